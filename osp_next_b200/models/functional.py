@@ -1,0 +1,201 @@
+"""Functional layer the DiT modules call.
+
+Three paths, chosen per call:
+
+* CPU tensors: plain differentiable PyTorch in the tensors' own dtype — the
+  reference's math without autocast, so fp32 CPU runs compare bit-for-bit-ish
+  with the reference model (tests/test_parity_reference.py).
+* CUDA, no autograd (sampling, RL rollouts): the fused sm_100a kernels of
+  :mod:`osp_next_b200.ops` (bf16 operands, fp32 accumulation, fp32 residual).
+* CUDA with autograd (training): :class:`torch.autograd.Function` wrappers whose
+  forward runs the same kernels; GEMM backward runs on the same tcgen05 GEMM
+  (on transposed operands); norm/RoPE backward is written in PyTorch.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from .. import ops
+from ..ops import reference as ref
+
+_BF16 = torch.bfloat16
+
+
+def _fused(*ts) -> bool:
+    """Fused kernel path: CUDA tensors and no autograd graph being built."""
+    t0 = next(t for t in ts if t is not None)
+    if not t0.is_cuda:
+        return False
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in ts):
+        return False
+    return True
+
+
+def _grad_cuda(*ts) -> bool:
+    t0 = next(t for t in ts if t is not None)
+    return t0.is_cuda and not _fused(*ts)
+
+
+# ----------------------------------------------------------------------------- GEMM autograd
+
+class _LinearFn(torch.autograd.Function):
+    """y = act(x·Wᵀ + b) with forward and backward GEMMs on the tcgen05 kernel."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, act):
+        x2 = x.reshape(-1, x.shape[-1]).to(_BF16)
+        wb = w.to(_BF16)
+        if act == "gelu_tanh":
+            pre = ops.linear(x2, wb, b, None, out_dtype=torch.float32)
+            y = F.gelu(pre, approximate="tanh").to(_BF16)
+            ctx.save_for_backward(x2, wb, pre)
+        else:
+            y = ops.linear(x2, wb, b, None)
+            ctx.save_for_backward(x2, wb, None)
+        ctx.act = act
+        ctx.has_b = b is not None
+        ctx.in_shape = x.shape
+        ctx.w_dtype = w.dtype
+        ctx.x_dtype = x.dtype
+        return y.view(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, gy):
+        x2, wb, pre = ctx.saved_tensors
+        g = gy.reshape(-1, gy.shape[-1])
+        if ctx.act == "gelu_tanh":
+            with torch.enable_grad():
+                p = pre.detach().requires_grad_(True)
+                out = F.gelu(p, approximate="tanh")
+                (g,) = torch.autograd.grad(out, p, g.float())
+        gb = g.to(_BF16)
+        # dX = dY·W  → GEMM(dY, Wᵀ) ; dW = dYᵀ·X → GEMM(dYᵀ, Xᵀ)
+        dx = ops.linear(gb, wb.t().contiguous(), None, None, out_dtype=torch.float32)
+        dw = ops.linear(gb.t().contiguous(), x2.t().contiguous(), None, None, out_dtype=torch.float32)
+        db = g.float().sum(0) if ctx.has_b else None
+        return dx.view(ctx.in_shape).to(ctx.x_dtype), dw.to(ctx.w_dtype), db, None
+
+
+def linear(x, w, b=None, act: Optional[str] = None):
+    if not x.is_cuda:
+        y = F.linear(x, w.to(x.dtype), None if b is None else b.to(x.dtype))
+        return F.gelu(y, approximate="tanh") if act == "gelu_tanh" else y
+    if _fused(x, w, b):
+        return ops.linear(x, w, b, act)
+    return _LinearFn.apply(x, w, b, act)
+
+
+def gated_residual_linear(x, w, b, resid, gate=None):
+    """resid + (x·Wᵀ + b)·gate  (gate [B,C] or None)."""
+    if not x.is_cuda:
+        y = F.linear(x, w.to(x.dtype), None if b is None else b.to(x.dtype))
+        return resid + (y * gate[:, None, :] if gate is not None else y)
+    if _fused(x, w, b, resid, gate):
+        # in place on the fp32 residual: each output row is read and written by one thread
+        out = resid if (resid.dtype == torch.float32 and resid.is_contiguous()) else None
+        return ops.linear_gated_residual(x, w, b, resid, gate, out=out)
+    y = _LinearFn.apply(x, w, b, None)
+    y = y.float()
+    return resid.float() + (y * gate.float()[:, None, :] if gate is not None else y)
+
+
+# ----------------------------------------------------------------------------- norms
+
+def ln_modulate(x, shift, scale, eps):
+    if not x.is_cuda:
+        y = F.layer_norm(x.float(), (x.shape[-1],), eps=eps).type_as(x)
+        return y * (1 + scale[:, None, :]) + shift[:, None, :]
+    if _fused(x, shift, scale):
+        return ops.ln_modulate(x, shift, scale, eps)
+    y = F.layer_norm(x.float(), (x.shape[-1],), eps=eps)
+    return (y * (1 + scale.float()[:, None, :]) + shift.float()[:, None, :]).to(_BF16)
+
+
+def layer_norm(x, weight, bias, eps):
+    if not x.is_cuda:
+        return F.layer_norm(x.float(), (x.shape[-1],), weight, bias, eps).type_as(x)
+    if _fused(x, weight, bias):
+        return ops.layer_norm(x, weight, bias, eps)
+    w = weight.float() if weight is not None else None
+    b = bias.float() if bias is not None else None
+    return F.layer_norm(x.float(), (x.shape[-1],), w, b, eps).to(_BF16)
+
+
+def rms_norm(x, weight, eps):
+    if not x.is_cuda:
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).type_as(x) * weight
+    if _fused(x, weight):
+        return ops.rms_norm(x, weight, eps)
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)) * weight.float()
+
+
+def apply_rope(x, pos, freqs):
+    """x [B,n,H,D] → rotated fp32 (CPU / autograd path)."""
+    return ref.apply_rope(x, pos, freqs)
+
+
+# ----------------------------------------------------------------------------- attention
+
+class _AttnFn(torch.autograd.Function):
+    """Segmented attention: forward on the tcgen05 flash kernel, backward by
+    recomputation of each segment with exact softmax gradients in fp32 blocks."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, seg_q, seg_k, scale):
+        o, lse = ops.attention(q.to(_BF16), k.to(_BF16), v.to(_BF16), seg_q, seg_k, scale, return_lse=True)
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.seg_q = seg_q.tolist()
+        ctx.seg_k = seg_k.tolist()
+        ctx.scale = scale
+        return o
+
+    @staticmethod
+    def backward(ctx, go):
+        q, k, v, o, lse = ctx.saved_tensors
+        dq = torch.zeros_like(q, dtype=torch.float32)
+        dk = torch.zeros_like(k, dtype=torch.float32)
+        dv = torch.zeros_like(v, dtype=torch.float32)
+        sq, sk = ctx.seg_q, ctx.seg_k
+        scale = ctx.scale
+        # delta_i = rowsum(dO ∘ O)
+        delta = (go.float() * o.float()).sum(-1).transpose(1, 2)          # B,H,nq
+        QB = 2048
+        for s in range(len(sq) - 1):
+            ks = k[:, sk[s]:sk[s + 1]].float().transpose(1, 2)            # B,H,Lk,D
+            vs = v[:, sk[s]:sk[s + 1]].float().transpose(1, 2)
+            for q0 in range(sq[s], sq[s + 1], QB):
+                q1 = min(q0 + QB, sq[s + 1])
+                qs = q[:, q0:q1].float().transpose(1, 2)
+                g = go[:, q0:q1].float().transpose(1, 2)
+                p = torch.exp(qs @ ks.transpose(-1, -2) * scale - lse[:, :, q0:q1, None])
+                dv[:, sk[s]:sk[s + 1]] += (p.transpose(-1, -2) @ g).transpose(1, 2)
+                dp = g @ vs.transpose(-1, -2)
+                ds = p * (dp - delta[:, :, q0:q1, None]) * scale
+                dq[:, q0:q1] = (ds @ ks).transpose(1, 2)
+                dk[:, sk[s]:sk[s + 1]] += (ds.transpose(-1, -2) @ qs).transpose(1, 2)
+        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, None, None
+
+
+def attention(q, k, v, seg_q, seg_k, scale=None):
+    """Attention inside segments; q [B,nq,H,D], k/v [B,nk,H,D] → [B,nq,H,D]."""
+    D = q.shape[-1]
+    scale = scale if scale is not None else 1.0 / math.sqrt(D)
+    if not q.is_cuda:
+        B, nq, H, _ = q.shape
+        outs = []
+        sq, sk = seg_q.tolist(), seg_k.tolist()
+        for s in range(len(sq) - 1):
+            qs = q[:, sq[s]:sq[s + 1]].transpose(1, 2)
+            ks = k[:, sk[s]:sk[s + 1]].transpose(1, 2)
+            vs = v[:, sk[s]:sk[s + 1]].transpose(1, 2)
+            outs.append(F.scaled_dot_product_attention(qs, ks, vs, scale=scale).transpose(1, 2))
+        return torch.cat(outs, dim=1)
+    if _fused(q, k, v):
+        return ops.attention(q, k, v, seg_q, seg_k, scale)
+    return _AttnFn.apply(q, k, v, seg_q, seg_k, scale)

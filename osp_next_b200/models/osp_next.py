@@ -1,0 +1,508 @@
+"""OSP-Next DiT: Wan-2.1-shaped transformer with Skiparse-2D sparse blocks.
+
+Parameter names and shapes equal the reference's (ospnext/modules/osp_next.py:
+1025-1376, want2v.py:262-287) so Wan-2.1 / OSP-Next checkpoints load unchanged:
+``patch_embedding``, ``text_embedding.{0,2}``, ``time_embedding.{0,2}``,
+``time_projection.1``, ``blocks.{i}.{norm3, modulation, self_attn.{q,k,v,o,norm_q,
+norm_k}, cross_attn.{…}, ffn.{0,2}}``, ``head.{head, modulation}``.
+
+What differs from the reference is *how* a block runs (the math is the same):
+
+* the residual stream of a rank is the ordered token list of its current
+  :class:`~osp_next_b200.models.layout.TokenLayout`; Skiparse groups are
+  contiguous attention segments, never a permuted copy of the batch, and the
+  layout change between Token and Group blocks is stored directly by the
+  FFN-down GEMM epilogue (single GPU) or by the SSP exchange (several GPUs);
+* q/k/v come from one fused GEMM with a concatenated ``[3C, C]`` weight, followed
+  by one fused full-row RMSNorm + 3-D RoPE pass;
+* cond/uncond CFG passes run as one batch of 2 (or on two GPU sets);
+* the residual stream is fp32 and the time modulation is computed in fp32.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import List, Optional, Tuple
+
+import torch
+import torch.nn as nn
+import torch.utils.checkpoint
+
+from . import functional as Fn
+from .layout import (FULL, GROUP, TOKEN, ParallelSpec, TokenLayout, block_schedule,
+                     make_layout, make_redistribution, token_positions)
+from ..ops import reference as ref
+
+
+# ----------------------------------------------------------------------------- helpers
+
+def sinusoidal_embedding_1d(dim: int, position: torch.Tensor) -> torch.Tensor:
+    """``[cos, sin](t·10000^(−i/half))`` computed in float64 (want2v.py:17-28)."""
+    assert dim % 2 == 0
+    half = dim // 2
+    position = position.type(torch.float64)
+    sinusoid = torch.outer(position, torch.pow(10000, -torch.arange(half).to(position).div(half)))
+    return torch.cat([torch.cos(sinusoid), torch.sin(sinusoid)], dim=1)
+
+
+class WanRMSNorm(nn.Module):
+    """RMSNorm over the full row with an fp32 weight (want2v.py:77-93)."""
+
+    def __init__(self, dim, eps=1e-5):
+        super().__init__()
+        self.dim = dim
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x):
+        return Fn.rms_norm(x, self.weight, self.eps)
+
+    def reset_parameters(self):
+        nn.init.ones_(self.weight)
+
+
+class WanLayerNorm(nn.LayerNorm):
+    """LayerNorm computed in fp32 (want2v.py:96-106)."""
+
+    def __init__(self, dim, eps=1e-6, elementwise_affine=False):
+        super().__init__(dim, elementwise_affine=elementwise_affine, eps=eps)
+
+    def forward(self, x):
+        return Fn.layer_norm(x, self.weight, self.bias, self.eps)
+
+
+@dataclass
+class BlockContext:
+    """Everything a block needs besides its weights, for one forward pass."""
+    layout: TokenLayout
+    pos: torch.Tensor                 # int32 [n_local, 3] true (t,h,w) of each local row
+    seg: torch.Tensor                 # int32 attention segments over layout.attn_tokens
+    freqs: torch.Tensor               # fp32 RoPE angle table
+    ulysses_group: object = None      # process group for the head all-to-all (None: none)
+    next_dest_row: Optional[torch.Tensor] = None   # fuse the layout change into FFN-down (1 GPU)
+    next_n: int = 0
+
+
+class OSPNextSelfAttention(nn.Module):
+    def __init__(self, dim, num_heads, window_size=(-1, -1), qk_norm=True, eps=1e-6, **kwargs):
+        super().__init__()
+        assert dim % num_heads == 0
+        self.dim = dim
+        self.num_heads = num_heads
+        self.head_dim = dim // num_heads
+        self.window_size = window_size
+        self.qk_norm = qk_norm
+        self.eps = eps
+        make_linear = kwargs.get("make_linear", nn.Linear)
+        self.q = make_linear(dim, dim)
+        self.k = make_linear(dim, dim)
+        self.v = make_linear(dim, dim)
+        self.o = make_linear(dim, dim)
+        self.norm_q = WanRMSNorm(dim, eps=eps) if qk_norm else nn.Identity()
+        self.norm_k = WanRMSNorm(dim, eps=eps) if qk_norm else nn.Identity()
+        self._packed = None
+        self.quant_attn = kwargs.get("quant_attn")
+
+    # fused [3C, C] weight for the inference path; rebuilt when any source changes
+    def packed_qkv(self):
+        ws = (self.q.weight, self.k.weight, self.v.weight)
+        bs = (self.q.bias, self.k.bias, self.v.bias)
+        key = tuple((t.data_ptr(), t._version) for t in ws + bs)
+        if self._packed is None or self._packed[0] != key:
+            W = torch.cat([w.detach() for w in ws], 0).to(torch.bfloat16).contiguous()
+            b = torch.cat([x.detach() for x in bs], 0).float().contiguous()
+            self._packed = (key, W, b)
+        return self._packed[1], self._packed[2]
+
+    def _qkv(self, x, ctx: BlockContext):
+        B, n, _ = x.shape
+        H, D = self.num_heads, self.head_dim
+        lora = any(hasattr(m, "lora_A") for m in (self.q, self.k, self.v))
+        if Fn._fused(x, self.q.weight) and self.qk_norm and not lora and not _hif8(self):
+            W, b = self.packed_qkv()
+            qkv = Fn.ops.linear(x, W, b)
+            return Fn.ops.qk_norm_rope(qkv, self.norm_q.weight, self.norm_k.weight, ctx.pos, ctx.freqs, H, self.eps)
+        q = self.norm_q(self.q(x)).view(B, n, H, D)
+        k = self.norm_k(self.k(x)).view(B, n, H, D)
+        v = self.v(x).view(B, n, H, D)
+        q = Fn.apply_rope(q, ctx.pos, ctx.freqs)
+        k = Fn.apply_rope(k, ctx.pos, ctx.freqs)
+        dt = torch.bfloat16 if x.is_cuda else v.dtype
+        return q.to(dt), k.to(dt), v.to(dt)
+
+    def forward(self, x, ctx: BlockContext):
+        """x: modulated-normalised input [B, n_local, C] → attention output [B, n_local, C]."""
+        q, k, v = self._qkv(x, ctx)
+        if ctx.ulysses_group is not None:
+            from ..parallel.comm import ulysses_all_to_all
+            q = ulysses_all_to_all(q, ctx.ulysses_group, ctx.layout.a2a_splits, True)
+            k = ulysses_all_to_all(k, ctx.ulysses_group, ctx.layout.a2a_splits, True)
+            v = ulysses_all_to_all(v, ctx.ulysses_group, ctx.layout.a2a_splits, True)
+        if self.quant_attn == "hif8":
+            from ..quant.hif8 import hif8_qkv
+            q, k, v = hif8_qkv(q, k, v, getattr(self, "scale_max_forward", 15.0),
+                               getattr(self, "scale_max_backward", 224.0))
+        o = Fn.attention(q, k, v, ctx.seg, ctx.seg)
+        if ctx.ulysses_group is not None:
+            from ..parallel.comm import ulysses_all_to_all
+            o = ulysses_all_to_all(o, ctx.ulysses_group, ctx.layout.a2a_splits, False)
+        return o.flatten(2)
+
+
+def _hif8(attn) -> bool:
+    return getattr(attn.q, "is_hif8", False)
+
+
+class OSPNextCrossAttention(OSPNextSelfAttention):
+    def text_kv(self, text):
+        B, L, _ = text.shape
+        H, D = self.num_heads, self.head_dim
+        k = self.norm_k(self.k(text)).view(B, L, H, D)
+        v = self.v(text).view(B, L, H, D)
+        return k, v
+
+    def forward(self, x, text, kv=None):
+        B, n, _ = x.shape
+        H, D = self.num_heads, self.head_dim
+        q = self.norm_q(self.q(x)).view(B, n, H, D)
+        k, v = kv if kv is not None else self.text_kv(text)
+        if self.quant_attn == "hif8":
+            from ..quant.hif8 import hif8_qkv
+            q, k, v = hif8_qkv(q, k, v, getattr(self, "scale_max_forward", 15.0),
+                               getattr(self, "scale_max_backward", 224.0))
+        seg_q = torch.tensor([0, n], dtype=torch.int32)
+        seg_k = torch.tensor([0, k.shape[1]], dtype=torch.int32)
+        if x.is_cuda:
+            q, k, v = q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16)
+        return Fn.attention(q, k, v, seg_q, seg_k).flatten(2)
+
+
+class OSPNextAttentionBlock(nn.Module):
+    def __init__(self, dim, ffn_dim, num_heads, window_size=(-1, -1), qk_norm=True, cross_attn_norm=False,
+                 eps=1e-6, sparse_ratio=2, skiparse_block_type=FULL, is_full2skiparse_block=False,
+                 is_skiparse2full_block=False, quant=None, quant_attn=None, scale_max_forward=15.0,
+                 scale_max_backward=224.0):
+        super().__init__()
+        self.dim = dim
+        self.ffn_dim = ffn_dim
+        self.num_heads = num_heads
+        self.eps = eps
+        self.cross_attn_norm = cross_attn_norm
+        make_linear = _linear_factory(quant, scale_max_forward, scale_max_backward)
+        kw = dict(make_linear=make_linear, quant_attn=quant_attn)
+        self.norm1 = WanLayerNorm(dim, eps)
+        self.self_attn = OSPNextSelfAttention(dim, num_heads, window_size, qk_norm, eps, **kw)
+        self.norm3 = WanLayerNorm(dim, eps, elementwise_affine=True) if cross_attn_norm else nn.Identity()
+        self.cross_attn = OSPNextCrossAttention(dim, num_heads, window_size, qk_norm, eps, **kw)
+        self.norm2 = WanLayerNorm(dim, eps)
+        self.ffn = nn.Sequential(make_linear(dim, ffn_dim), nn.GELU(approximate="tanh"), make_linear(ffn_dim, dim))
+        self.modulation = nn.Parameter(torch.randn(1, 6, dim) / dim ** 0.5)
+        for a in (self.self_attn, self.cross_attn):
+            a.scale_max_forward = scale_max_forward
+            a.scale_max_backward = scale_max_backward
+        self.sparse_ratio = sparse_ratio
+        self.skiparse_block_type = skiparse_block_type
+        self.is_full2skiparse_block = is_full2skiparse_block
+        self.is_skiparse2full_block = is_skiparse2full_block
+
+    def reset_parameters(self):
+        with torch.no_grad():
+            self.modulation.copy_(torch.randn_like(self.modulation) / self.dim ** 0.5)
+
+    def block_forward(self, x, e0, text, ctx: BlockContext, text_kv=None):
+        e = (self.modulation.float() + e0.float())                      # [B,6,C]
+        e = [e[:, i] for i in range(6)]
+        # self-attention
+        xm = Fn.ln_modulate(x, e[0], e[1], self.eps)
+        y = self.self_attn(xm, ctx)
+        x = Fn.gated_residual_linear(y, self.self_attn.o.weight, self.self_attn.o.bias, x, e[2]) \
+            if _plain(self.self_attn.o) else x + self.self_attn.o(y) * e[2][:, None, :]
+        # cross-attention
+        xn = self.norm3(x) if self.cross_attn_norm else (x if not x.is_cuda else x.to(torch.bfloat16))
+        y = self.cross_attn(xn, text, text_kv)
+        x = Fn.gated_residual_linear(y, self.cross_attn.o.weight, self.cross_attn.o.bias, x, None) \
+            if _plain(self.cross_attn.o) else x + self.cross_attn.o(y)
+        # FFN
+        xm = Fn.ln_modulate(x, e[3], e[4], self.eps)
+        f0, f2 = self.ffn[0], self.ffn[2]
+        if _plain(f0):
+            h = Fn.linear(xm, f0.weight, f0.bias, act="gelu_tanh")
+        else:
+            h = self.ffn[1](f0(xm))
+        if _plain(f2) and ctx.next_dest_row is not None and Fn._fused(h, f2.weight, x):
+            # layout change for the next block fused into the FFN-down store
+            return Fn.ops.linear_gated_residual(h, f2.weight, f2.bias, x, e[5],
+                                                dest_row=ctx.next_dest_row, n_out=ctx.next_n)
+        if _plain(f2):
+            x = Fn.gated_residual_linear(h, f2.weight, f2.bias, x, e[5])
+        else:
+            x = x + f2(h) * e[5][:, None, :]
+        return x
+
+    def forward(self, x, e0, text, ctx: BlockContext, text_kv=None, gradient_checkpointing=False):
+        if gradient_checkpointing and torch.is_grad_enabled():
+            lora = [p for n_, p in self.named_parameters() if "lora_" in n_]
+
+            def run(x_, e0_, text_, *lora_dummy):
+                return self.block_forward(x_, e0_, text_, ctx, text_kv)
+            return torch.utils.checkpoint.checkpoint(run, x, e0, text, *lora, use_reentrant=False)
+        return self.block_forward(x, e0, text, ctx, text_kv)
+
+
+def _plain(m) -> bool:
+    """A plain nn.Linear (no LoRA / HiF8 wrapper) can use the fused GEMM epilogues."""
+    return type(m) is nn.Linear
+
+
+def _linear_factory(quant, smf, smb):
+    if quant == "hif8":
+        from ..quant.hif8 import HIF8Linear
+
+        def mk(i, o, bias=True):
+            return HIF8Linear(i, o, bias=bias, scale_max_forward=smf, scale_max_backward=smb)
+        return mk
+    return nn.Linear
+
+
+class Head(nn.Module):
+    """Output head: LN + modulation + Linear(C → prod(patch)·out) (want2v.py:262-287)."""
+
+    def __init__(self, dim, out_dim, patch_size, eps=1e-6):
+        super().__init__()
+        self.dim = dim
+        self.out_dim = out_dim
+        self.patch_size = patch_size
+        self.eps = eps
+        self.norm = WanLayerNorm(dim, eps)
+        self.head = nn.Linear(dim, math.prod(patch_size) * out_dim)
+        self.modulation = nn.Parameter(torch.randn(1, 2, dim) / dim ** 0.5)
+
+    def forward(self, x, e):
+        m = self.modulation.float() + e.float()[:, None, :]
+        xm = Fn.ln_modulate(x, m[:, 0], m[:, 1], self.eps)
+        return Fn.linear(xm, self.head.weight, self.head.bias)
+
+
+class OSPNextModel(nn.Module):
+    """OSP-Next DiT (registry name ``osp_next``)."""
+
+    def __init__(self, model_type="t2v", patch_size=(1, 2, 2), text_len=512, in_dim=16, dim=2048, ffn_dim=8192,
+                 freq_dim=256, text_dim=4096, out_dim=16, num_heads=16, num_layers=32, window_size=(-1, -1),
+                 qk_norm=True, cross_attn_norm=True, eps=1e-6, skiparse_model_type="full", sparse_ratio=2,
+                 num_full_blocks=0, quant=None, quant_attn=None, scale_max_forward=15.0, scale_max_backward=224.0,
+                 **kwargs):
+        super().__init__()
+        assert model_type in ("t2v", "i2v")
+        self.model_type = model_type
+        self.patch_size = tuple(patch_size)
+        self.text_len = text_len
+        self.in_dim = in_dim
+        self.dim = dim
+        self.ffn_dim = ffn_dim
+        self.freq_dim = freq_dim
+        self.text_dim = text_dim
+        self.out_dim = out_dim
+        self.num_heads = num_heads
+        self.num_layers = num_layers
+        self.window_size = window_size
+        self.qk_norm = qk_norm
+        self.cross_attn_norm = cross_attn_norm
+        self.eps = eps
+        self.quant = quant
+        self.quant_attn = quant_attn
+        self.gradient_checkpointing = False
+        self.config = dict(model_type=model_type, patch_size=list(self.patch_size), text_len=text_len, in_dim=in_dim,
+                           dim=dim, ffn_dim=ffn_dim, freq_dim=freq_dim, text_dim=text_dim, out_dim=out_dim,
+                           num_heads=num_heads, num_layers=num_layers, qk_norm=qk_norm,
+                           cross_attn_norm=cross_attn_norm, eps=eps, skiparse_model_type=skiparse_model_type,
+                           sparse_ratio=sparse_ratio, num_full_blocks=num_full_blocks, quant=quant,
+                           quant_attn=quant_attn, scale_max_forward=scale_max_forward,
+                           scale_max_backward=scale_max_backward)
+
+        self.patch_embedding = nn.Conv3d(in_dim, dim, kernel_size=patch_size, stride=patch_size)
+        self.text_embedding = nn.Sequential(nn.Linear(text_dim, dim), nn.GELU(approximate="tanh"), nn.Linear(dim, dim))
+        self.time_embedding = nn.Sequential(nn.Linear(freq_dim, dim), nn.SiLU(), nn.Linear(dim, dim))
+        self.time_projection = nn.Sequential(nn.SiLU(), nn.Linear(dim, dim * 6))
+
+        self.skiparse_model_type = skiparse_model_type
+        self.sparse_ratio = 1 if skiparse_model_type == "full" else sparse_ratio
+        kinds, full_idx = block_schedule(num_layers, skiparse_model_type, num_full_blocks)
+        self.num_full_blocks = len(full_idx)
+        self.block_kinds = kinds
+        self.full_block_indices = full_idx
+        self.blocks = nn.ModuleList()
+        for i, kind in enumerate(kinds):
+            prev_full = i == 0 or kinds[i - 1] == FULL
+            next_full = i == num_layers - 1 or kinds[i + 1] == FULL
+            self.blocks.append(OSPNextAttentionBlock(
+                dim, ffn_dim, num_heads, window_size, qk_norm, cross_attn_norm, eps,
+                sparse_ratio=self.sparse_ratio if kind != FULL else 1, skiparse_block_type=kind,
+                is_full2skiparse_block=kind != FULL and prev_full, is_skiparse2full_block=kind != FULL and next_full,
+                quant=quant, quant_attn=quant_attn, scale_max_forward=scale_max_forward,
+                scale_max_backward=scale_max_backward))
+        self.head = Head(dim, out_dim, self.patch_size, eps)
+        assert dim % num_heads == 0 and (dim // num_heads) % 2 == 0
+        self.rope_d = dim // num_heads
+        self._freqs = None
+        self.parallel: Optional["SPRuntime"] = None      # set by parallel.sp.attach_sp
+        self._text_kv_cache = None
+        self.init_weights()
+
+    # ------------------------------------------------------------------ misc API
+    def set_gradient_checkpointing(self, enabled=False):
+        self.gradient_checkpointing = enabled
+
+    def reset_parameters(self):
+        self.init_weights()
+
+    def init_weights(self):
+        for n, m in self.named_modules():
+            if n and hasattr(m, "reset_parameters"):
+                m.reset_parameters()
+
+    @property
+    def dtype(self):
+        return self.patch_embedding.weight.dtype
+
+    def freqs(self, device):
+        if self._freqs is None or self._freqs.device != torch.device(device):
+            self._freqs = ref.rope_freqs(self.rope_d).to(device)
+        return self._freqs
+
+    def enable_text_kv_cache(self, enabled: bool = True):
+        """Cache cross-attention K/V of the text per block (constant across sampler steps)."""
+        self._text_kv_cache = {} if enabled else None
+
+    # ------------------------------------------------------------------ embeddings
+    def patchify_embed(self, x):
+        """Conv3d(k=s=patch) as one GEMM over flattened patches → [B, N, C], grid."""
+        B, Cin, T, H, W = x.shape
+        pt, ph, pw = self.patch_size
+        grid = (T // pt, H // ph, W // pw)
+        w = self.patch_embedding.weight
+        if not x.is_cuda:
+            y = self.patch_embedding(x.to(w.dtype))
+            return y.flatten(2).transpose(1, 2), grid
+        p = x.view(B, Cin, grid[0], pt, grid[1], ph, grid[2], pw).permute(0, 2, 4, 6, 1, 3, 5, 7)
+        p = p.reshape(B, grid[0] * grid[1] * grid[2], Cin * pt * ph * pw).to(torch.bfloat16)
+        y = Fn.linear(p, w.reshape(w.shape[0], -1), self.patch_embedding.bias)
+        return y.float(), grid
+
+    def unpatchify(self, x, grid):
+        """b (f h w) (x y z c) -> b c (f x) (h y) (w z) (osp_next.py:1349-1368)."""
+        B = x.shape[0]
+        f, h, w = grid
+        pt, ph, pw = self.patch_size
+        c = self.out_dim
+        x = x.view(B, f, h, w, pt, ph, pw, c).permute(0, 7, 1, 4, 2, 5, 3, 6)
+        return x.reshape(B, c, f * pt, h * ph, w * pw)
+
+    def time_embed(self, t):
+        tf = sinusoidal_embedding_1d(self.freq_dim, t).float()
+        te0, te2 = self.time_embedding[0], self.time_embedding[2]
+        e = torch.nn.functional.linear(tf, te0.weight.float(), te0.bias.float())
+        e = torch.nn.functional.linear(torch.nn.functional.silu(e), te2.weight.float(), te2.bias.float())
+        tp = self.time_projection[1]
+        e0 = torch.nn.functional.linear(torch.nn.functional.silu(e), tp.weight.float(), tp.bias.float())
+        return e, e0.unflatten(1, (6, self.dim))
+
+    def text_embed(self, text):
+        l0, l2 = self.text_embedding[0], self.text_embedding[2]
+        h = Fn.linear(text.to(l0.weight.dtype) if not text.is_cuda else text, l0.weight, l0.bias, act="gelu_tanh")
+        return Fn.linear(h, l2.weight, l2.bias)
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, x, t, text, **kwargs):
+        """x [B,C,T,H,W] latents, t [B] timesteps (σ·1000), text [B,L,text_dim] → velocity fp32."""
+        device = x.device
+        x, grid = self.patchify_embed(x)
+        e, e0 = self.time_embed(t.to(device))
+        text = self.text_embed(text)
+        rt = self.parallel
+        spec = rt.spec if rt is not None else ParallelSpec()
+        P = self.sparse_ratio
+        freqs = self.freqs(device)
+
+        prev_kind = None
+        # rows of the first layout (every rank computed the full patch embedding)
+        first = make_layout(self.block_kinds[0], grid, P, spec)
+        x = x[:, first.tokens.to(device)] if not _is_arange(first.tokens, x.shape[1]) else x
+        prev_kind = self.block_kinds[0]
+        nb = len(self.blocks)
+        for i, block in enumerate(self.blocks):
+            kind = self.block_kinds[i]
+            if kind != prev_kind:
+                x = self._redistribute(x, prev_kind, kind, grid, spec)
+            prev_kind = kind
+            ctx = self._context(kind, grid, spec, device, freqs)
+            nxt = self.block_kinds[i + 1] if i + 1 < nb else None
+            fuse = (spec.world == 1 and nxt is not None and nxt != kind and x.is_cuda
+                    and not (torch.is_grad_enabled() and self.training))
+            if fuse:
+                rd = make_redistribution(kind, nxt, grid, P, spec)
+                ctx.next_dest_row = _dev(rd.dest_row, device, torch.int32)
+                ctx.next_n = rd.n_out
+            kv = None
+            if self._text_kv_cache is not None and not torch.is_grad_enabled():
+                key = (i, text.data_ptr(), text.shape)
+                kv = self._text_kv_cache.get(key)
+                if kv is None:
+                    kv = block.cross_attn.text_kv(text)
+                    self._text_kv_cache[key] = kv
+            x = block(x, e0, text, ctx, kv, gradient_checkpointing=self.gradient_checkpointing)
+            if fuse:
+                prev_kind = nxt
+        x = self.head(x, e)
+        # back to natural order, full sequence on every rank
+        x = self._gather_natural(x, prev_kind, grid, spec)
+        return self.unpatchify(x, grid).float()
+
+    def _context(self, kind, grid, spec, device, freqs) -> BlockContext:
+        lay = make_layout(kind, grid, self.sparse_ratio, spec)
+        pos = _dev(token_positions(lay.tokens, grid), device, torch.int32)
+        seg = lay.seg
+        ug = None
+        if lay.a2a_splits is not None and self.parallel is not None:
+            ug = self.parallel.full_group if kind == FULL or self.sparse_ratio == 1 else self.parallel.ulysses_group
+        return BlockContext(layout=lay, pos=pos, seg=seg, freqs=freqs, ulysses_group=ug)
+
+    def _redistribute(self, x, ka, kb, grid, spec):
+        rd = make_redistribution(ka, kb, grid, self.sparse_ratio, spec)
+        if spec.world == 1:
+            return x if rd.identity else x[:, _dev(rd.gather, x.device, torch.long)]
+        from ..parallel.redistribute import redistribute
+        return redistribute(x, rd, self.parallel.global_sp_group)
+
+    def _gather_natural(self, x, kind, grid, spec):
+        lay = make_layout(kind, grid, self.sparse_ratio, spec)
+        N = grid[0] * grid[1] * grid[2]
+        if spec.world == 1:
+            if _is_arange(lay.tokens, N):
+                return x
+            out = x.new_empty(x.shape[0], N, x.shape[2])
+            out[:, _dev(lay.tokens, x.device, torch.long)] = x
+            return out
+        from ..parallel.redistribute import gather_natural
+        return gather_natural(x, kind, grid, self.sparse_ratio, spec, self.parallel.global_sp_group)
+
+
+def _is_arange(idx: torch.Tensor, n: int) -> bool:
+    return idx.numel() == n and bool(torch.equal(idx, torch.arange(n, dtype=idx.dtype)))
+
+
+_DEV_CACHE = {}
+
+
+def _dev(t: torch.Tensor, device, dtype):
+    key = (id(t), str(device), dtype)
+    v = _DEV_CACHE.get(key)
+    if v is None or v[0] is not t:
+        v = (t, t.to(device=device, dtype=dtype))
+        _DEV_CACHE[key] = v
+    return v[1]
+
+
+models = {"osp_next": OSPNextModel}
+models_main_block = {"osp_next": OSPNextAttentionBlock}
+models_blocks_to_float = {"osp_next": [WanLayerNorm, WanRMSNorm]}
+models_blocks_to_output_float = {"osp_next": None}

@@ -1,0 +1,169 @@
+"""Fused ops of the OSP-Next DiT.
+
+Every op has one CUDA implementation (hand-written sm_100a kernels in
+``ops/csrc``, loaded from the in-tree ``_C.so``) and a PyTorch reference used for
+CPU tensors and as the numerics oracle in tests (:mod:`.reference`).  There is
+no silent fallback on CUDA tensors: a missing extension raises.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from . import reference as ref
+from ._ext import ext, available  # noqa: F401
+
+_BF16 = torch.bfloat16
+
+
+def _cuda(*ts) -> bool:
+    return any(t is not None and t.is_cuda for t in ts)
+
+
+def _c(t):
+    return t if t is None or t.is_contiguous() else t.contiguous()
+
+
+# ----------------------------------------------------------------------------- norms
+
+def ln_modulate(x, shift, scale, eps: float = 1e-6):
+    """bf16 ``LN(x)·(1+scale)+shift`` (x fp32/bf16 [B,n,C], shift/scale [B,C])."""
+    if not _cuda(x):
+        return ref.ln_modulate(x, shift, scale, eps)
+    x = _c(x)
+    out = torch.empty(x.shape, dtype=_BF16, device=x.device)
+    ext().ln_modulate(x, _c(shift.float()), _c(scale.float()), None, None, out, float(eps))
+    return out
+
+
+def layer_norm(x, weight, bias, eps: float = 1e-6):
+    """bf16 affine LayerNorm (fp32 math)."""
+    if not _cuda(x):
+        return ref.layer_norm(x, weight, bias, eps)
+    x = _c(x)
+    out = torch.empty(x.shape, dtype=_BF16, device=x.device)
+    w = weight.float().contiguous() if weight is not None else None
+    b = bias.float().contiguous() if bias is not None else None
+    ext().ln_modulate(x, None, None, w, b, out, float(eps))
+    return out
+
+
+def rms_norm(x, weight, eps: float = 1e-6):
+    """bf16 row RMSNorm over the last dim (the full 5120-wide row for q/k)."""
+    if not _cuda(x):
+        return ref.rms_norm(x, weight, eps)
+    x = _c(x)
+    out = torch.empty(x.shape, dtype=_BF16, device=x.device)
+    ext().rms_norm(x, weight.float().contiguous() if weight is not None else None, out, float(eps))
+    return out
+
+
+# ----------------------------------------------------------------------------- GEMMs
+
+def linear(x, weight, bias=None, act: Optional[str] = None, out_dtype=_BF16):
+    """``act(x·Wᵀ+b)`` on the tcgen05 GEMM (bf16 in, fp32 accumulate in TMEM)."""
+    if not _cuda(x):
+        return ref.linear(x, weight, bias, act, out_dtype)
+    shp = x.shape
+    a = _c(x.reshape(-1, shp[-1]).to(_BF16))
+    w = _c(weight.to(_BF16))
+    out = torch.empty(a.shape[0], w.shape[0], dtype=out_dtype, device=x.device)
+    ext().gemm(a, w, None if bias is None else bias.float().contiguous(), out,
+               1 if act == "gelu_tanh" else 0, None, None, None, 0, 0)
+    return out.view(*shp[:-1], w.shape[0])
+
+
+def linear_gated_residual(x, weight, bias, resid, gate=None, dest_row=None, n_out=None, out=None):
+    """``resid + (x·Wᵀ+b)·gate`` with fp32 residual, optional row remap on store.
+
+    x [B,n,K] bf16, resid [B,n,C] fp32 (may alias ``out`` when no remap),
+    gate [B,C] or None.  ``dest_row`` [n] int: row m of each batch entry is stored
+    at ``dest_row[m]`` of the [B,n_out,C] output (layout change fused in the store).
+    """
+    if not _cuda(x):
+        return ref.linear_gated_residual(x, weight, bias, resid, gate, dest_row, n_out)
+    B, n, K = x.shape
+    a = _c(x.reshape(B * n, K).to(_BF16))
+    w = _c(weight.to(_BF16))
+    C = w.shape[0]
+    resid = _c(resid.float())
+    if dest_row is None:
+        if out is None:
+            out = resid
+        n_out = n
+        dr = None
+    else:
+        if out is None:
+            out = torch.empty(B, n_out, C, dtype=torch.float32, device=x.device)
+        dr = dest_row.to(device=x.device, dtype=torch.int32).contiguous()
+    ext().gemm(a, w, None if bias is None else bias.float().contiguous(), out.view(-1, C), 0,
+               resid.view(-1, C), None if gate is None else gate.float().contiguous(), dr, n, n_out)
+    return out
+
+
+# ----------------------------------------------------------------------------- attention
+
+def qk_norm_rope(qkv, wq, wk, pos, freqs, num_heads: int, eps: float = 1e-6):
+    """Fused full-row RMSNorm(q), RMSNorm(k) and 3-D RoPE on a fused qkv buffer.
+
+    CUDA: in place on ``qkv`` [B,n,3C] bf16; returns (q,k,v) as strided views
+    [B,n,H,D] into it.  ``pos`` int32 [n,3]; ``freqs`` fp32 angle table.
+    """
+    if not _cuda(qkv):
+        return ref.qk_norm_rope(qkv, wq, wk, pos, freqs, num_heads, eps)
+    B, n, C3 = qkv.shape
+    C = C3 // 3
+    D = C // num_heads
+    ext().qk_norm_rope(qkv, wq.float().contiguous(), wk.float().contiguous(),
+                       pos.to(device=qkv.device, dtype=torch.int32).contiguous(),
+                       freqs.to(device=qkv.device, dtype=torch.float32).contiguous(), num_heads, float(eps))
+    q, k, v = qkv.split(C, dim=-1)
+    return q.view(B, n, num_heads, D), k.view(B, n, num_heads, D), v.view(B, n, num_heads, D)
+
+
+def attention(q, k, v, seg_q, seg_k, scale: Optional[float] = None, return_lse: bool = False):
+    """Segmented non-causal attention on the tcgen05 flash kernel.
+
+    q [B,nq,H,D], k/v [B,nk,H,D] (row-strided views allowed; last dim contiguous).
+    Returns o [B,nq,H,D] bf16 contiguous (+ LSE [B,H,nq] fp32).
+    """
+    D = q.shape[-1]
+    scale = scale if scale is not None else 1.0 / math.sqrt(D)
+    if not _cuda(q):
+        return ref.attention(q, k, v, seg_q, seg_k, scale, return_lse)
+    B, nq, H, _ = q.shape
+    out = torch.empty(B, nq, H, D, dtype=_BF16, device=q.device)
+    lse = torch.empty(B, H, nq, dtype=torch.float32, device=q.device)
+    ext().attention_fwd(q, k, v, seg_q.to(device=q.device, dtype=torch.int32).contiguous(),
+                        seg_k.to(device=q.device, dtype=torch.int32).contiguous(), out, lse, float(scale))
+    return (out, lse) if return_lse else out
+
+
+# ----------------------------------------------------------------------------- sampler / quant
+
+def cfg_euler_step(latents, cond, uncond, guidance: float, dt: float):
+    if not _cuda(latents):
+        return ref.cfg_euler_step(latents, cond, uncond, guidance, dt)
+    out = torch.empty_like(latents)
+    ext().cfg_euler(_c(latents), _c(cond), _c(uncond), out, float(guidance), float(dt))
+    return out
+
+
+def hif8_round(x):
+    if not _cuda(x):
+        return ref.hif8_round(x)
+    out = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+    ext().hif8_round(_c(x.float()), out, 1.0)
+    return out
+
+
+def hif8_quant_dequant(x, scale_max: float = 15.0):
+    """Per-tensor scaled HiF8 fake-quant; amax on device, no host sync."""
+    if not _cuda(x):
+        return ref.hif8_quant_dequant(x, scale_max)
+    xc = _c(x)
+    out = torch.empty_like(xc)
+    ext().hif8_qdq(xc, out, float(scale_max))
+    return out
