@@ -107,3 +107,21 @@ def import_reference(disable_compile: bool = False, force_sdpa: bool = False):
     import ospnext.modules.osp_next as osp
     import ospnext.schedulers.flow_matching as fm
     return osp, fm
+
+
+def fa2_usable() -> bool:
+    """True when the installed flash_attn (FA2) runs on the current GPU.
+
+    The reference prefers FA2 when importable (attention.py:8-27); its wheel may
+    lack kernels for this architecture, in which case the reference's own SDPA
+    branch is used instead (attention.py:479).
+    """
+    try:
+        import torch
+        from flash_attn import flash_attn_func
+        q = torch.randn(1, 128, 1, 64, device="cuda", dtype=torch.bfloat16)
+        flash_attn_func(q, q, q)
+        torch.cuda.synchronize()
+        return True
+    except Exception:
+        return False

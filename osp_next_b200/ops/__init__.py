@@ -123,11 +123,32 @@ def qk_norm_rope(qkv, wq, wk, pos, freqs, num_heads: int, eps: float = 1e-6):
     return q.view(B, n, num_heads, D), k.view(B, n, num_heads, D), v.view(B, n, num_heads, D)
 
 
+_SEG_CACHE = {}
+
+
+def _seg_dev(seg: torch.Tensor, device):
+    """Device copy (int32) and max segment length of a CPU segment table, cached."""
+    if seg.is_cuda:
+        return seg.to(torch.int32), int((seg[1:] - seg[:-1]).max().item())
+    key = (seg.data_ptr(), seg.numel(), str(device))
+    hit = _SEG_CACHE.get(key)
+    if hit is not None and hit[0] is seg:
+        return hit[1], hit[2]
+    d = seg.to(device=device, dtype=torch.int32)
+    mx = int((seg[1:] - seg[:-1]).max().item()) if seg.numel() > 1 else 0
+    if len(_SEG_CACHE) > 256:
+        _SEG_CACHE.clear()
+    _SEG_CACHE[key] = (seg, d, mx)
+    return d, mx
+
+
 def attention(q, k, v, seg_q, seg_k, scale: Optional[float] = None, return_lse: bool = False):
     """Segmented non-causal attention on the tcgen05 flash kernel.
 
-    q [B,nq,H,D], k/v [B,nk,H,D] (row-strided views allowed; last dim contiguous).
-    Returns o [B,nq,H,D] bf16 contiguous (+ LSE [B,H,nq] fp32).
+    q [B,nq,H,D], k/v [B,nk,H,D] (row-strided views allowed; heads packed, last
+    dim contiguous).  ``seg_q``/``seg_k`` int32 offsets (CPU tensors preferred:
+    the device copy is cached).  Returns o [B,nq,H,D] bf16 contiguous
+    (+ LSE [B,H,nq] fp32, natural log).
     """
     D = q.shape[-1]
     scale = scale if scale is not None else 1.0 / math.sqrt(D)
@@ -135,10 +156,30 @@ def attention(q, k, v, seg_q, seg_k, scale: Optional[float] = None, return_lse: 
         return ref.attention(q, k, v, seg_q, seg_k, scale, return_lse)
     B, nq, H, _ = q.shape
     out = torch.empty(B, nq, H, D, dtype=_BF16, device=q.device)
-    lse = torch.empty(B, H, nq, dtype=torch.float32, device=q.device)
-    ext().attention_fwd(q, k, v, seg_q.to(device=q.device, dtype=torch.int32).contiguous(),
-                        seg_k.to(device=q.device, dtype=torch.int32).contiguous(), out, lse, float(scale))
+    lse = torch.empty(B, H, nq, dtype=torch.float32, device=q.device) if return_lse else torch.empty(0, device=q.device)
+    sq, max_q = _seg_dev(seg_q, q.device)
+    sk, _ = _seg_dev(seg_k, q.device)
+    ext().attention_fwd(q, k, v, sq, sk, out, lse, float(scale), max_q)
     return (out, lse) if return_lse else out
+
+
+def sde_step(x, v, sigma: float, dt: float, sigma_min: float, sigma_max: float, noise=None, prev_sample=None):
+    """Fused GRPO SDE step (CUDA) → (prev_sample f32, log_prob [B] f32, mean f32)."""
+    x = _c(x.float())
+    v = _c(v.float())
+    prev = torch.empty_like(x)
+    mean = torch.empty_like(x)
+    logp = torch.zeros(x.shape[0], dtype=torch.float32, device=x.device)
+    ext().sde_step(x, v, None if noise is None else _c(noise.float()),
+                   None if prev_sample is None else _c(prev_sample.float()), prev, mean, logp,
+                   float(sigma), float(dt), float(sigma_min), float(sigma_max))
+    return prev, logp, mean
+
+
+def adamw_(p, g, m, v, lr, beta1, beta2, eps, weight_decay, step, grad_scale=1.0):
+    """In-place fused AdamW on flat fp32 shards (CUDA)."""
+    ext().adamw(p, _c(g), m, v, float(lr), float(beta1), float(beta2), float(eps), float(weight_decay), int(step),
+                float(grad_scale))
 
 
 # ----------------------------------------------------------------------------- sampler / quant

@@ -9,6 +9,29 @@ import os
 
 _EXT = None
 _ERR = None
+_LAUNCHES = [0]
+
+
+class _Counted:
+    """Proxy over the extension module that counts kernel-launching calls."""
+
+    def __init__(self, mod):
+        self._mod = mod
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if name.startswith("get_"):
+            return fn
+
+        def call(*a, **k):
+            _LAUNCHES[0] += 1
+            return fn(*a, **k)
+        return call
+
+
+def launch_count() -> int:
+    """Number of extension kernel calls made so far in this process."""
+    return _LAUNCHES[0]
 
 
 def ext():
@@ -17,7 +40,7 @@ def ext():
         return _EXT
     try:
         import torch  # noqa: F401  (libtorch must be loaded before the extension)
-        _EXT = importlib.import_module("osp_next_b200.ops._C")
+        _EXT = _Counted(importlib.import_module("osp_next_b200.ops._C"))
     except ImportError as e:  # pragma: no cover - exercised only on misconfigured boxes
         _ERR = e
         raise RuntimeError(

@@ -1,0 +1,68 @@
+// Python bindings of the sm_100a kernels (module osp_next_b200.ops._C).
+#include <torch/extension.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime.h>
+#include <mutex>
+
+#include "tma_host.h"
+
+namespace osp {
+void gemm(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& bias, at::Tensor& out,
+          int64_t act, const c10::optional<at::Tensor>& resid, const c10::optional<at::Tensor>& gate,
+          const c10::optional<at::Tensor>& dest_row, int64_t rows_per_batch, int64_t n_out);
+void ln_modulate(const at::Tensor& x, const c10::optional<at::Tensor>& shift, const c10::optional<at::Tensor>& scale,
+                 const c10::optional<at::Tensor>& w, const c10::optional<at::Tensor>& b, at::Tensor& out, double eps);
+void rms_norm(const at::Tensor& x, const c10::optional<at::Tensor>& w, at::Tensor& out, double eps);
+void qk_norm_rope(at::Tensor& qkv, const at::Tensor& wq, const at::Tensor& wk, const at::Tensor& pos,
+                  const at::Tensor& freqs, int64_t num_heads, double eps);
+void attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& seg_q,
+                   const at::Tensor& seg_k, at::Tensor& out, at::Tensor& lse, double scale, int64_t max_q);
+void cfg_euler(const at::Tensor& lat, const at::Tensor& cond, const at::Tensor& unc, at::Tensor& out, double g,
+               double dt);
+void hif8_round(const at::Tensor& x, at::Tensor& out, double s);
+void hif8_qdq(const at::Tensor& x, at::Tensor& out, double scale_max);
+void adamw(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, double lr, double b1, double b2,
+           double eps, double wd, int64_t step, double gscale);
+void sde_step(const at::Tensor& x, const at::Tensor& v, const c10::optional<at::Tensor>& xi,
+              const c10::optional<at::Tensor>& prev_in, at::Tensor& prev_out, const c10::optional<at::Tensor>& mean_out,
+              at::Tensor& logp, double sigma, double dt, double smin, double smax);
+
+static int* g_err[64] = {nullptr};
+static std::mutex g_err_mu;
+
+int* error_word(int device) {
+  std::lock_guard<std::mutex> lk(g_err_mu);
+  if (!g_err[device]) {
+    c10::cuda::CUDAGuard guard(device);
+    C10_CUDA_CHECK(cudaMalloc(&g_err[device], sizeof(int)));
+    C10_CUDA_CHECK(cudaMemset(g_err[device], 0, sizeof(int)));
+  }
+  return g_err[device];
+}
+
+// Read (and optionally clear) the first error code recorded by a bounded device wait.
+int64_t get_error(int64_t device, bool clear) {
+  int* w = error_word((int)device);
+  int h = 0;
+  c10::cuda::CUDAGuard guard((int)device);
+  C10_CUDA_CHECK(cudaDeviceSynchronize());
+  C10_CUDA_CHECK(cudaMemcpy(&h, w, sizeof(int), cudaMemcpyDeviceToHost));
+  if (clear) C10_CUDA_CHECK(cudaMemset(w, 0, sizeof(int)));
+  return h;
+}
+}  // namespace osp
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "OSP-Next B200 kernels (sm_100a: tcgen05 GEMM + flash attention, fused elementwise)";
+  m.def("gemm", &osp::gemm);
+  m.def("ln_modulate", &osp::ln_modulate);
+  m.def("rms_norm", &osp::rms_norm);
+  m.def("qk_norm_rope", &osp::qk_norm_rope);
+  m.def("attention_fwd", &osp::attention_fwd);
+  m.def("cfg_euler", &osp::cfg_euler);
+  m.def("hif8_round", &osp::hif8_round);
+  m.def("hif8_qdq", &osp::hif8_qdq);
+  m.def("adamw", &osp::adamw);
+  m.def("sde_step", &osp::sde_step);
+  m.def("get_error", &osp::get_error, pybind11::arg("device"), pybind11::arg("clear") = true);
+}

@@ -1,0 +1,359 @@
+// Persistent warp-specialised tcgen05 GEMM for sm_100a:  D[M,N] = A[M,K] · B[N,K]ᵀ
+// (nn.Linear layout: activations and weights both K-major, bf16), fp32 accumulation
+// in TMEM, fused epilogues.
+//
+// Reference hot ops this replaces (all cuBLAS + eager elementwise there):
+//   q/k/v/o, cross-attn, FFN linears of OSPNextAttentionBlock
+//   (ospnext/modules/osp_next.py:742-777, 873-877, 926-957), text/patch
+//   embeddings and the head (osp_next.py:1092-1104, 1249-1252, want2v.py:262-287).
+//
+// Structure (one CTA per SM, 192 threads):
+//   warp 0      TMA producer: A/B k-blocks into a STAGES-deep smem ring (128B swizzle)
+//   warp 1      MMA issuer:  tcgen05.mma 128×BN×16 per step into one of two TMEM
+//               accumulators (so the epilogue of tile i overlaps the MMAs of tile i+1)
+//   warps 2..5  epilogue:    tcgen05.ld 32 columns at a time, bias / GELU-tanh /
+//               gated fp32 residual (+ row remap = fused layout change), global store
+// Tiles are visited in M-groups of 16 so the weight stays L2-resident across a group.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+#include "tma_host.h"
+
+namespace osp {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;              // 64 bf16 = 128 B rows (one swizzle span)
+constexpr int kGroupM = 16;
+constexpr int kSmemBudget = 196608;  // 192 KiB of operand ring
+
+enum EpiMode : int { kEpiStore = 0, kEpiResidual = 1 };
+
+struct GemmArgs {
+  int M, N, K;
+  const float* bias;        // [N] or null
+  int act;                  // 0 none, 1 gelu_tanh
+  void* out;                // [M or B*n_out, N] (bf16 or f32)
+  const float* resid;       // [M, N] f32 (residual mode)
+  const float* gate;        // [B, N] f32 or null (residual mode)
+  const int* dest_row;      // [rows_per_batch] or null
+  int rows_per_batch;       // n (residual mode)
+  int n_out;                // rows per batch of out (residual mode with dest_row)
+  int* err;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
+  const int per_group = kGroupM * num_n;
+  const int g = t / per_group;
+  const int first_m = g * kGroupM;
+  const int gsize = min(num_m - first_m, kGroupM);
+  const int r = t - g * per_group;
+  mb = first_m + r % gsize;
+  nb = r / gsize;
+}
+
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+  const float k0 = 0.7978845608028654f;   // sqrt(2/pi)
+  const float k1 = 0.044715f;
+  return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+}
+
+template <int BN, int MODE, typename OutT>
+__global__ void __launch_bounds__(192, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
+  constexpr int STAGES = kSmemBudget / (kBM * kBK * 2 + BN * kBK * 2);
+  constexpr uint32_t A_BYTES = kBM * kBK * 2;
+  constexpr uint32_t B_BYTES = BN * kBK * 2;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr uint32_t IDESC = idesc_bf16(kBM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base_u32 = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (base_u32 & 1023u)) & 1023u);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int num_m = (args.M + kBM - 1) / kBM;
+  const int num_n = (args.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (args.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], 4); }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, args.err, kErrGemmProducer)) { *abort_flag = 1; break; }
+          mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
+          tma_load_2d(&tmA, &full[stage], sA + stage * A_BYTES, kb * kBK, mb * kBM);
+          tma_load_2d(&tmB, &full[stage], sB + stage * B_BYTES, kb * kBK, nb * BN);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, args.err, kErrGemmMma)) { *abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, args.err, kErrGemmMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = sdesc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(b_addr + k * 32, 16, 1024);
+            umma_bf16(d_tmem, ad, bd, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        umma_commit(&tfull[acc]);
+        if (!ok) { *abort_flag = 1; break; }
+      }
+      // all MMAs issued by this thread done before teardown
+      umma_commit(done);
+      mbar_wait(done, 0, args.err, kErrGemmTeardown);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    const int quarter = warp & 3;               // TMEM lanes 32·quarter .. +31
+    int it = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+      if (*abort_flag) break;
+      int mb, nb;
+      tile_coords(t, num_m, num_n, mb, nb);
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogue))) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int row = mb * kBM + quarter * 32 + lane;
+      const bool row_ok = row < args.M;
+      long out_row = row;
+      int bidx = 0;
+      if (MODE == kEpiResidual && row_ok) {
+        bidx = row / args.rows_per_batch;
+        if (args.dest_row) {
+          const int m = row - bidx * args.rows_per_batch;
+          out_row = (long)bidx * args.n_out + args.dest_row[m];
+        }
+      }
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int col0 = nb * BN + c * 32;
+        uint32_t r[32];
+        tmem_ld32(t_row + c * 32, r);
+        tmem_ld_wait();
+        if (!row_ok || col0 >= args.N) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (args.bias) {
+          const float4* b4 = reinterpret_cast<const float4*>(args.bias + col0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float4 b = __ldg(b4 + j);
+            v[4 * j] += b.x; v[4 * j + 1] += b.y; v[4 * j + 2] += b.z; v[4 * j + 3] += b.w;
+          }
+        }
+        if (MODE == kEpiStore) {
+          if (args.act == 1) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_f(v[j]);
+          }
+          OutT* o = reinterpret_cast<OutT*>(args.out) + out_row * args.N + col0;
+          if constexpr (sizeof(OutT) == 2) {
+            uint4* o4 = reinterpret_cast<uint4*>(o);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint4 w;
+              w.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+              w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+              w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+              w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+              o4[j] = w;
+            }
+          } else {
+            float4* o4 = reinterpret_cast<float4*>(o);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          }
+        } else {
+          // resid + bf16(y)·gate  (the Linear output is bf16 under autocast in the reference)
+          const float4* r4 = reinterpret_cast<const float4*>(args.resid + (long)row * args.N + col0);
+          float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + out_row * args.N + col0);
+          const float4* g4 = args.gate ? reinterpret_cast<const float4*>(args.gate + (long)bidx * args.N + col0)
+                                       : nullptr;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float4 x = r4[j];
+            float4 g = g4 ? __ldg(g4 + j) : make_float4(1.f, 1.f, 1.f, 1.f);
+            x.x += bf16_round(v[4 * j + 0]) * g.x;
+            x.y += bf16_round(v[4 * j + 1]) * g.y;
+            x.z += bf16_round(v[4 * j + 2]) * g.z;
+            x.w += bf16_round(v[4 * j + 3]) * g.w;
+            o4[j] = x;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+template <int BN>
+constexpr int gemm_smem_bytes() {
+  constexpr int STAGES = kSmemBudget / (kBM * kBK * 2 + BN * kBK * 2);
+  return 1024 + STAGES * (kBM * kBK * 2 + BN * kBK * 2) + (2 * STAGES + 5) * 8 + 16;
+}
+
+static int num_sms(int dev) {
+  static int cache[64] = {0};
+  if (!cache[dev]) cudaDeviceGetAttribute(&cache[dev], cudaDevAttrMultiProcessorCount, dev);
+  return cache[dev];
+}
+
+template <int BN, int MODE, typename OutT>
+static void launch_gemm(const at::Tensor& a, const at::Tensor& b, GemmArgs& args, cudaStream_t stream) {
+  CUtensorMap tmA = make_tmap_2d_bf16(a.data_ptr(), args.K, args.M, a.stride(0), kBK, kBM);
+  CUtensorMap tmB = make_tmap_2d_bf16(b.data_ptr(), args.K, args.N, b.stride(0), kBK, BN);
+  auto kern = gemm_kernel<BN, MODE, OutT>;
+  constexpr int smem = gemm_smem_bytes<BN>();
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured = true;
+  }
+  const int tiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
+  const int grid = std::max(1, std::min(tiles, num_sms(a.get_device())));
+  kern<<<grid, 192, smem, stream>>>(tmA, tmB, args);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// out = act(a·bᵀ + bias)  or  out[remap] = resid + (a·bᵀ + bias)·gate
+void gemm(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& bias, at::Tensor& out,
+          int64_t act, const c10::optional<at::Tensor>& resid, const c10::optional<at::Tensor>& gate,
+          const c10::optional<at::Tensor>& dest_row, int64_t rows_per_batch, int64_t n_out) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "gemm: CUDA tensors expected");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm: bf16 operands");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1), "gemm: a [M,K], b [N,K]");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1, "gemm: operands must be K-contiguous");
+  TORCH_CHECK(a.size(1) % 8 == 0, "gemm: K must be a multiple of 8 (16-byte TMA rows)");
+  TORCH_CHECK((a.stride(0) * 2) % 16 == 0 && (b.stride(0) * 2) % 16 == 0, "gemm: row strides 16-byte aligned");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(a.data_ptr()) % 16 == 0 &&
+              reinterpret_cast<uintptr_t>(b.data_ptr()) % 16 == 0, "gemm: 16-byte aligned operands");
+  TORCH_CHECK(b.size(0) % 32 == 0, "gemm: N must be a multiple of 32");
+  TORCH_CHECK(out.is_contiguous(), "gemm: contiguous output");
+  c10::cuda::CUDAGuard guard(a.device());
+  GemmArgs args{};
+  args.M = (int)a.size(0);
+  args.N = (int)b.size(0);
+  args.K = (int)a.size(1);
+  args.bias = nullptr;
+  if (bias.has_value()) {
+    TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->is_contiguous() && bias->numel() == args.N,
+                "gemm: bias f32 [N]");
+    args.bias = bias->data_ptr<float>();
+  }
+  args.act = (int)act;
+  args.out = out.data_ptr();
+  args.err = error_word(a.get_device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (args.M == 0) return;
+  if (resid.has_value()) {
+    TORCH_CHECK(out.scalar_type() == at::kFloat && resid->scalar_type() == at::kFloat && resid->is_contiguous(),
+                "gemm: residual mode is fp32");
+    TORCH_CHECK(resid->numel() == (int64_t)args.M * args.N, "gemm: resid [M,N]");
+    args.resid = resid->data_ptr<float>();
+    args.gate = nullptr;
+    args.rows_per_batch = (int)rows_per_batch;
+    TORCH_CHECK(rows_per_batch > 0 && args.M % rows_per_batch == 0, "gemm: M = B·rows_per_batch");
+    if (gate.has_value()) {
+      TORCH_CHECK(gate->scalar_type() == at::kFloat && gate->is_contiguous() &&
+                  gate->numel() == (int64_t)(args.M / rows_per_batch) * args.N, "gemm: gate f32 [B,N]");
+      args.gate = gate->data_ptr<float>();
+    }
+    args.dest_row = nullptr;
+    args.n_out = (int)n_out;
+    if (dest_row.has_value()) {
+      TORCH_CHECK(dest_row->scalar_type() == at::kInt && dest_row->numel() == rows_per_batch,
+                  "gemm: dest_row int32 [n]");
+      TORCH_CHECK(out.numel() == (int64_t)(args.M / rows_per_batch) * n_out * args.N, "gemm: out [B,n_out,N]");
+      args.dest_row = dest_row->data_ptr<int>();
+    } else {
+      TORCH_CHECK(out.numel() == (int64_t)args.M * args.N, "gemm: out [M,N]");
+    }
+    if (args.N % 256 == 0) launch_gemm<256, kEpiResidual, float>(a, b, args, stream);
+    else if (args.N % 128 == 0) launch_gemm<128, kEpiResidual, float>(a, b, args, stream);
+    else launch_gemm<64, kEpiResidual, float>(a, b, args, stream);
+    return;
+  }
+  TORCH_CHECK(out.numel() == (int64_t)args.M * args.N, "gemm: out [M,N]");
+  if (out.scalar_type() == at::kBFloat16) {
+    if (args.N % 256 == 0) launch_gemm<256, kEpiStore, __nv_bfloat16>(a, b, args, stream);
+    else if (args.N % 128 == 0) launch_gemm<128, kEpiStore, __nv_bfloat16>(a, b, args, stream);
+    else launch_gemm<64, kEpiStore, __nv_bfloat16>(a, b, args, stream);
+  } else {
+    TORCH_CHECK(out.scalar_type() == at::kFloat, "gemm: out bf16 or f32");
+    if (args.N % 256 == 0) launch_gemm<256, kEpiStore, float>(a, b, args, stream);
+    else if (args.N % 128 == 0) launch_gemm<128, kEpiStore, float>(a, b, args, stream);
+    else launch_gemm<64, kEpiStore, float>(a, b, args, stream);
+  }
+}
+
+}  // namespace osp

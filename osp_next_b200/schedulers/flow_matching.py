@@ -109,18 +109,19 @@ class FlowMatchingScheduler:
         return latents, latents
 
     def sample(self, model, latents, prompt_embeds=None, negative_prompt_embeds=None,
-               step_callback: Optional[Callable] = None, cfg_parallel=None, **model_kwargs):
+               step_callback: Optional[Callable] = None, cfg_parallel=None, max_steps=None, **model_kwargs):
         """Euler sampling with CFG.
 
         ``cfg_parallel``: optional :class:`osp_next_b200.parallel.cfg.CFGParallel`
         that runs cond on one half of the ranks and uncond on the other.
+        ``max_steps``: stop after the first steps of the schedule (timing runs).
         """
         n = self.num_inference_steps
         sigmas = self._set_sigmas(training=False)
         timesteps = sigmas.clone() * 1000
         cfg = self.do_classifier_free_guidance and negative_prompt_embeds is not None
         g = self.guidance_scale
-        for i in range(n):
+        for i in range(n if max_steps is None else min(n, max_steps)):
             t = timesteps[i]
             dt_sigma = float(sigmas[i + 1] - sigmas[i])
             B = latents.shape[0]

@@ -1,0 +1,198 @@
+"""Numerics of every sm_100a kernel against the fp32 PyTorch reference of the same op.
+
+Shapes cover tile tails (M, N, K not multiples of the tile), both GEMM epilogues,
+Skiparse-style variable-length attention segments, head dims 64 and 128, and
+row-strided q/k/v views of a fused qkv buffer.
+"""
+import math
+
+import pytest
+import torch
+
+from osp_next_b200 import ops
+from osp_next_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _close(a, b, rtol, atol):
+    a = a.float()
+    b = b.float()
+    err = (a - b).abs()
+    tol = atol + rtol * b.abs()
+    bad = (err > tol).float().mean().item()
+    assert bad == 0.0, f"max err {err.max().item():.3e}, frac bad {bad:.2e}, max ref {b.abs().max().item():.3e}"
+
+
+def _no_device_error():
+    assert ops.ext().get_error(torch.cuda.current_device(), True) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 384, 200), (1000, 5120, 512), (77, 64, 4096),
+                                   (2048, 1536, 1536)])
+@pytest.mark.parametrize("act", [None, "gelu_tanh"])
+def test_gemm_store(M, N, K, act):
+    torch.manual_seed(0)
+    x = torch.randn(M, K, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=DEV) / math.sqrt(K)).to(torch.bfloat16)
+    b = torch.randn(N, device=DEV)
+    y = ops.linear(x, w, b, act)
+    r = ref.linear(x, w, b, act, out_dtype=torch.float32)
+    _close(y, r, 1e-2, 1e-2)
+    y32 = ops.linear(x, w, None, None, out_dtype=torch.float32)
+    _close(y32, ref.linear(x, w, None, None, out_dtype=torch.float32), 1e-4, 1e-3)
+    _no_device_error()
+
+
+@pytest.mark.parametrize("B,n,C,K", [(2, 200, 256, 512), (1, 1000, 1536, 1536), (2, 333, 5120, 640)])
+@pytest.mark.parametrize("remap", [False, True])
+def test_gemm_gated_residual(B, n, C, K, remap):
+    torch.manual_seed(1)
+    x = torch.randn(B, n, K, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(C, K, device=DEV) / math.sqrt(K)).to(torch.bfloat16)
+    b = torch.randn(C, device=DEV)
+    resid = torch.randn(B, n, C, device=DEV)
+    gate = torch.randn(B, C, device=DEV)
+    if remap:
+        perm = torch.randperm(n, device=DEV)
+        y = ops.linear_gated_residual(x, w, b, resid.clone(), gate, dest_row=perm, n_out=n)
+        r = ref.linear_gated_residual(x, w, b, resid, gate, dest_row=perm, n_out=n)
+    else:
+        y = ops.linear_gated_residual(x, w, b, resid.clone(), gate)
+        r = ref.linear_gated_residual(x, w, b, resid, gate)
+    _close(y, r, 1e-3, 2e-2)
+    _no_device_error()
+
+
+@pytest.mark.parametrize("B,n,C", [(2, 37, 5120), (1, 64, 256), (3, 5, 1536)])
+def test_norms(B, n, C):
+    torch.manual_seed(2)
+    x = torch.randn(B, n, C, device=DEV) * 3 + 1
+    sh, sc = torch.randn(B, C, device=DEV), torch.randn(B, C, device=DEV)
+    _close(ops.ln_modulate(x, sh, sc, 1e-6), ref.ln_modulate(x, sh, sc, 1e-6, torch.float32), 1e-2, 2e-2)
+    w, bb = torch.randn(C, device=DEV), torch.randn(C, device=DEV)
+    _close(ops.layer_norm(x, w, bb, 1e-6), ref.layer_norm(x, w, bb, 1e-6, torch.float32), 1e-2, 2e-2)
+    xb = x.to(torch.bfloat16)
+    _close(ops.rms_norm(xb, w, 1e-6), ref.rms_norm(xb, w, 1e-6, torch.float32), 1e-2, 2e-2)
+    _close(ops.ln_modulate(xb, sh, sc, 1e-6), ref.ln_modulate(xb, sh, sc, 1e-6, torch.float32), 1e-2, 3e-2)
+
+
+@pytest.mark.parametrize("H,D", [(40, 128), (4, 64), (2, 128)])
+def test_qk_norm_rope(H, D):
+    torch.manual_seed(3)
+    B, n = 2, 50
+    C = H * D
+    qkv = torch.randn(B, n, 3 * C, device=DEV).to(torch.bfloat16)
+    wq, wk = torch.rand(C, device=DEV) + 0.5, torch.rand(C, device=DEV) + 0.5
+    pos = torch.stack([torch.randint(0, 21, (n,)), torch.randint(0, 48, (n,)), torch.randint(0, 80, (n,))], 1)
+    freqs = ref.rope_freqs(D).to(DEV)
+    rq, rk, rv = ref.qk_norm_rope(qkv.clone(), wq, wk, pos.to(DEV), freqs, H)
+    q, k, v = ops.qk_norm_rope(qkv, wq, wk, pos.to(DEV), freqs, H)
+    _close(q, rq, 1e-2, 2e-2)
+    _close(k, rk, 1e-2, 2e-2)
+    _close(v, rv, 0, 0)
+
+
+def _segs(lengths):
+    s = [0]
+    for L in lengths:
+        s.append(s[-1] + L)
+    return torch.tensor(s, dtype=torch.int32)
+
+
+@pytest.mark.parametrize("D", [128, 64])
+@pytest.mark.parametrize("lengths", [[128], [256], [300], [1000, 1000, 1024, 977], [37, 1, 513]])
+def test_attention_segments(D, lengths):
+    torch.manual_seed(4)
+    B, H = 2, 3
+    n = sum(lengths)
+    q = torch.randn(B, n, H, D, device=DEV).to(torch.bfloat16)
+    k = torch.randn(B, n, H, D, device=DEV).to(torch.bfloat16)
+    v = torch.randn(B, n, H, D, device=DEV).to(torch.bfloat16)
+    seg = _segs(lengths)
+    o, lse = ops.attention(q, k, v, seg, seg, return_lse=True)
+    ro, rl = ref.attention(q, k, v, seg, seg, return_lse=True)
+    _close(o, ro.float(), 2e-2, 2e-2)
+    _close(lse, rl, 1e-3, 2e-3)
+    _no_device_error()
+
+
+def test_attention_cross_and_strided_views():
+    """Cross-attention (512 text keys) with q/k/v as strided views of fused buffers."""
+    torch.manual_seed(5)
+    B, n, L, H, D = 2, 700, 512, 4, 128
+    C = H * D
+    qkv = torch.randn(B, n, 3 * C, device=DEV).to(torch.bfloat16)
+    q, k, v = (t.view(B, n, H, D) for t in qkv.split(C, dim=-1))
+    seg = _segs([n])
+    _close(ops.attention(q, k, v, seg, seg), ref.attention(q, k, v, seg, seg).float(), 2e-2, 2e-2)
+    kv = torch.randn(B, L, 2 * C, device=DEV).to(torch.bfloat16)
+    kt, vt = (t.view(B, L, H, D) for t in kv.split(C, dim=-1))
+    sk = _segs([L])
+    _close(ops.attention(q, kt, vt, seg, sk), ref.attention(q, kt, vt, seg, sk).float(), 2e-2, 2e-2)
+    _no_device_error()
+
+
+def test_attention_large_scores():
+    """Scores with a large dynamic range exercise the lazy O rescaling."""
+    torch.manual_seed(6)
+    B, n, H, D = 1, 2048, 2, 128
+    q = (torch.randn(B, n, H, D, device=DEV) * 4).to(torch.bfloat16)
+    k = (torch.randn(B, n, H, D, device=DEV) * 4).to(torch.bfloat16)
+    k[:, 1500:1510] *= 3
+    v = torch.randn(B, n, H, D, device=DEV).to(torch.bfloat16)
+    seg = _segs([n])
+    _close(ops.attention(q, k, v, seg, seg), ref.attention(q, k, v, seg, seg).float(), 2e-2, 2e-2)
+
+
+def test_cfg_euler():
+    torch.manual_seed(7)
+    lat = torch.randn(2, 16, 3, 8, 8, device=DEV).to(torch.bfloat16)
+    c, u = torch.randn_like(lat, dtype=torch.float32), torch.randn_like(lat, dtype=torch.float32)
+    _close(ops.cfg_euler_step(lat, c, u, 5.0, -0.02), ref.cfg_euler_step(lat, c, u, 5.0, -0.02), 1e-2, 1e-2)
+    lat32 = lat.float()
+    _close(ops.cfg_euler_step(lat32, c, u, 5.0, -0.02), ref.cfg_euler_step(lat32, c, u, 5.0, -0.02), 1e-6, 1e-6)
+
+
+def test_hif8_matches_kernel_semantics():
+    """All 65 536 bf16 bit patterns plus random fp32: CUDA == reference restatement."""
+    allbf = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16).float()
+    allbf = allbf[torch.isfinite(allbf)]
+    r = torch.randn(1 << 20) * torch.exp(torch.randn(1 << 20) * 4)
+    for x in (allbf, r):
+        got = ops.hif8_round(x.to(DEV)).cpu()
+        exp = ref.hif8_round(x)
+        same = (got == exp) | (torch.isnan(got) & torch.isnan(exp))
+        assert bool(same.all()), x[~same][:8]
+    x = torch.randn(4096, device=DEV).to(torch.bfloat16)
+    _close(ops.hif8_quant_dequant(x, 15.0), ref.hif8_quant_dequant(x.cpu(), 15.0).to(DEV), 0, 0)
+
+
+def test_adamw_matches_torch():
+    torch.manual_seed(8)
+    p = torch.randn(10000, device=DEV)
+    p_ref = p.clone().requires_grad_(True)
+    opt = torch.optim.AdamW([p_ref], lr=1e-3, betas=(0.9, 0.999), eps=1e-15, weight_decay=0.01)
+    m, v = torch.zeros_like(p), torch.zeros_like(p)
+    for step in range(1, 4):
+        g = torch.randn_like(p)
+        p_ref.grad = g.clone()
+        opt.step()
+        ops.adamw_(p, g, m, v, 1e-3, 0.9, 0.999, 1e-15, 0.01, step)
+    _close(p, p_ref.detach(), 1e-5, 1e-6)
+
+
+def test_sde_step_matches_reference():
+    from osp_next_b200.rl.grpo import sde_step_with_logprob
+    torch.manual_seed(9)
+    sig = torch.linspace(1, 0, 17, device=DEV)
+    x = torch.randn(2, 16, 3, 8, 8, device=DEV)
+    v = torch.randn_like(x)
+    prev = torch.randn_like(x)
+    i = 3
+    p_ref, lp_ref, mean_ref, _ = sde_step_with_logprob(sig, v, i, x, 16, prev_sample=prev, use_kernel=False)
+    p, lp, mean = ops.sde_step(x, v, float(sig[i]), float(sig[i + 1] - sig[i]), float(sig[-1]), float(sig[0]),
+                               prev_sample=prev)
+    _close(mean, mean_ref, 1e-5, 1e-5)
+    _close(lp, lp_ref, 1e-4, 1e-4)
