@@ -122,9 +122,9 @@ class OSPNextSelfAttention(nn.Module):
             W, b = self.packed_qkv()
             qkv = Fn.ops.linear(x, W, b)
             return Fn.ops.qk_norm_rope(qkv, self.norm_q.weight, self.norm_k.weight, ctx.pos, ctx.freqs, H, self.eps)
-        q = self.norm_q(self.q(x)).view(B, n, H, D)
-        k = self.norm_k(self.k(x)).view(B, n, H, D)
-        v = self.v(x).view(B, n, H, D)
+        q = self.norm_q(_lin(self.q, x)).view(B, n, H, D)
+        k = self.norm_k(_lin(self.k, x)).view(B, n, H, D)
+        v = _lin(self.v, x).view(B, n, H, D)
         q = Fn.apply_rope(q, ctx.pos, ctx.freqs)
         k = Fn.apply_rope(k, ctx.pos, ctx.freqs)
         dt = torch.bfloat16 if x.is_cuda else v.dtype
@@ -153,18 +153,26 @@ def _hif8(attn) -> bool:
     return getattr(attn.q, "is_hif8", False)
 
 
+def _lin(mod, x):
+    """Plain Linears go through the functional layer (fused GEMM / dtype handling);
+    wrapped ones (LoRA, HiF8) run their own forward."""
+    if type(mod) is nn.Linear:
+        return Fn.linear(x, mod.weight, mod.bias)
+    return mod(x)
+
+
 class OSPNextCrossAttention(OSPNextSelfAttention):
     def text_kv(self, text):
         B, L, _ = text.shape
         H, D = self.num_heads, self.head_dim
-        k = self.norm_k(self.k(text)).view(B, L, H, D)
-        v = self.v(text).view(B, L, H, D)
+        k = self.norm_k(_lin(self.k, text)).view(B, L, H, D)
+        v = _lin(self.v, text).view(B, L, H, D)
         return k, v
 
     def forward(self, x, text, kv=None):
         B, n, _ = x.shape
         H, D = self.num_heads, self.head_dim
-        q = self.norm_q(self.q(x)).view(B, n, H, D)
+        q = self.norm_q(_lin(self.q, x)).view(B, n, H, D)
         k, v = kv if kv is not None else self.text_kv(text)
         if self.quant_attn == "hif8":
             from ..quant.hif8 import hif8_qkv

@@ -106,8 +106,8 @@ __global__ void absmax_kernel(const T* __restrict__ x, long n, unsigned* __restr
 template <typename T>
 __global__ void hif8_qdq_kernel(const T* __restrict__ x, T* __restrict__ out, long n, const unsigned* amax_bits,
                                 float scale_max) {
-  const float amax = __uint_as_float(*amax_bits);
-  const float s = amax > 0.f ? scale_max / amax : 1.f;
+  const float amax = fmaxf(__uint_as_float(*amax_bits), 1e-8f);    // x.abs().amax().clamp(min=1e-8)
+  const float s = scale_max / amax;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
     stf(out, i, hif8_round_dev(ldf(x, i) * s) / s);
 }

@@ -175,8 +175,8 @@ def hif8_quant_dequant(x: torch.Tensor, scale_max: float = 15.0) -> torch.Tensor
     step ``2^(max(e,−22) − m)``; round half away from zero; |v| < 2⁻²³ → 0;
     |v| ≥ 40960 → ±inf.  See :func:`hif8_round` for the grid alone.
     """
-    amax = x.detach().abs().max().float()
-    s = torch.where(amax > 0, scale_max / amax, torch.ones_like(amax))
+    amax = x.detach().abs().max().float().clamp(min=1e-8)
+    s = scale_max / amax
     y = hif8_round(x.float() * s) / s
     return y.to(x.dtype)
 

@@ -1,0 +1,204 @@
+"""HiF8 fake quantisation: linear layers, attention inputs, and the quantiser API.
+
+Reference: ospnext/modules/hif8_linear.py:42-170 and hif8_attention.py:40-127
+(per-tensor dynamic scale ``s = scale_max / max(|x|, 1e-8)``, quantise→dequantise
+x and W in forward, the incoming gradient in backward, straight-through
+estimator; q/k/v quantised before attention and dq/dk/dv after), plus the
+``quant_cy_npu`` surface those files import (QTensor.quant_dequant_float,
+QType, QLinear, replace_linear).  The reference can only run this on Ascend
+NPUs; here the rounding is the sm_100a kernel in ops/csrc/misc.cu (same grid as
+the Ascend kernel) and the matmuls are the tcgen05 GEMM.  GEMMs stay bf16: the
+reference emulates HiF8, it has no 8-bit matmul.
+"""
+from __future__ import annotations
+
+from copy import deepcopy
+from typing import List, Optional, Union
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .. import ops
+from ..ops import reference as ref
+
+
+def quant(x: torch.Tensor, scale_max: float) -> torch.Tensor:
+    """Scaled HiF8 quantise→dequantise of a whole tensor (device amax, no host sync)."""
+    if x.is_cuda:
+        return ops.hif8_quant_dequant(x.contiguous(), scale_max)
+    return ref.hif8_quant_dequant(x, scale_max)
+
+
+class _HIF8LinearFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias, smf: float, smb: float):
+        x_q = quant(x, smf)
+        w_q = quant(weight, smf)
+        ctx.save_for_backward(x_q, w_q)
+        ctx.smb = smb
+        ctx.has_bias = bias is not None
+        if x.is_cuda:
+            return ops.linear(x_q.reshape(-1, x.shape[-1]), w_q, bias).view(*x.shape[:-1], weight.shape[0])
+        return F.linear(x_q, w_q, bias)
+
+    @staticmethod
+    def backward(ctx, g):
+        x_q, w_q = ctx.saved_tensors
+        g_q = quant(g, ctx.smb)
+        g2 = g_q.reshape(-1, g_q.shape[-1])
+        x2 = x_q.reshape(-1, x_q.shape[-1])
+        if g.is_cuda:
+            gb = g2.to(torch.bfloat16)
+            dx = ops.linear(gb, w_q.to(torch.bfloat16).t().contiguous(), None, out_dtype=torch.float32)
+            dw = ops.linear(gb.t().contiguous(), x2.to(torch.bfloat16).t().contiguous(), None, out_dtype=torch.float32)
+        else:
+            dx = g2 @ w_q
+            dw = g2.t() @ x2
+        db = g2.float().sum(0) if ctx.has_bias else None
+        return dx.view(x_q.shape).to(x_q.dtype), dw.to(w_q.dtype), db, None, None
+
+
+class HIF8Linear(nn.Linear):
+    """Drop-in ``nn.Linear`` with HiF8 fake quantisation of x, W (forward) and dY (backward)."""
+    is_hif8 = True
+
+    def __init__(self, in_features, out_features, bias=True, scale_max_forward=15.0, scale_max_backward=224.0,
+                 device=None, dtype=None):
+        super().__init__(in_features, out_features, bias, device=device, dtype=dtype)
+        self.scale_max_forward = scale_max_forward
+        self.scale_max_backward = scale_max_backward
+        self._wq = None
+
+    def _cached_wq(self):
+        key = (self.weight.data_ptr(), self.weight._version)
+        if self._wq is None or self._wq[0] != key:
+            self._wq = (key, quant(self.weight.detach(), self.scale_max_forward).to(torch.bfloat16))
+        return self._wq[1]
+
+    def forward(self, x):
+        if x.is_cuda and not (torch.is_grad_enabled() and (x.requires_grad or self.weight.requires_grad)):
+            x_q = quant(x.to(torch.bfloat16), self.scale_max_forward)
+            return ops.linear(x_q.reshape(-1, x.shape[-1]), self._cached_wq(), self.bias).view(
+                *x.shape[:-1], self.out_features)
+        return _HIF8LinearFunction.apply(x, self.weight, self.bias, self.scale_max_forward, self.scale_max_backward)
+
+    def extra_repr(self):
+        return (f"in_features={self.in_features}, out_features={self.out_features}, bias={self.bias is not None}, "
+                f"scale_max_fwd={self.scale_max_forward}, scale_max_bwd={self.scale_max_backward}")
+
+
+class _HIF8QKV(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, smf, smb):
+        ctx.smb = smb
+        return quant(q, smf), quant(k, smf), quant(v, smf)
+
+    @staticmethod
+    def backward(ctx, gq, gk, gv):
+        f = (lambda g: None if g is None else quant(g.contiguous(), ctx.smb))
+        return f(gq), f(gk), f(gv), None, None
+
+
+def hif8_qkv(q, k, v, scale_max_forward=15.0, scale_max_backward=224.0):
+    """Quantise q/k/v (forward) and dq/dk/dv (backward) around any attention call."""
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
+        return _HIF8QKV.apply(q, k, v, scale_max_forward, scale_max_backward)
+    return quant(q, scale_max_forward), quant(k, scale_max_forward), quant(v, scale_max_forward)
+
+
+# ----------------------------------------------------------------------------- quantiser API
+
+class QType:
+    """Quantisation format descriptor (subset of quant_cy_npu/base/QType.py used by OSP-Next)."""
+
+    def __init__(self, desc: str):
+        if desc not in ("hif8", "bf16", "fp16", "fp32"):
+            raise ValueError(f"unsupported QType {desc!r}")
+        self.desc = desc
+        self.q_dim = -1
+
+    def dim(self, d):
+        out = deepcopy(self)
+        out.q_dim = d
+        return out
+
+    def dim_(self, d):
+        self.q_dim = d
+        return self
+
+    def copy(self):
+        return deepcopy(self)
+
+    def __repr__(self):
+        return f"QType: {self.desc}   Dim: {self.q_dim}"
+
+
+def quant_dequant_float(x: torch.Tensor, qtype: Union[QType, str], force_fp32: bool = False) -> torch.Tensor:
+    """Round ``x`` (already scaled) to the format's grid (QTensor.py:94-128 semantics)."""
+    desc = qtype if isinstance(qtype, str) else qtype.desc
+    if desc == "hif8":
+        y = ops.hif8_round(x.float().contiguous()) if x.is_cuda else ref.hif8_round(x)
+    elif desc == "bf16":
+        y = x.to(torch.bfloat16).float()
+    elif desc == "fp16":
+        y = x.to(torch.float16).float()
+    else:
+        y = x.float()
+    return y if force_fp32 else y.to(x.dtype)
+
+
+def quant_hif8(x: torch.Tensor) -> torch.Tensor:
+    """The reference's PyTorch formula (QFuncs/hif8.py:7-23), kept as a second oracle."""
+    return ref.hif8_round_torch_oracle(x)
+
+
+class QLinear(nn.Linear):
+    """Linear with fake-quantised weight / input / gradient (QLinear.py semantics, HiF8 grids)."""
+
+    def __init__(self, in_features, out_features, bias=True):
+        super().__init__(in_features, out_features, bias)
+        self.w_qtype: Optional[QType] = None
+        self.in_qtype: Optional[QType] = None
+        self.quant_grad = True
+
+    def transfer(self, m: nn.Linear):
+        with torch.no_grad():
+            self.weight.copy_(m.weight)
+            if m.bias is not None:
+                self.bias.copy_(m.bias)
+
+    def assign_qparams(self, q):
+        self.w_qtype = QType(q) if isinstance(q, str) else q
+
+    def assign_input_qparams(self, q):
+        self.in_qtype = QType(q) if isinstance(q, str) else q
+
+    def set_quant_grad(self, flag: bool):
+        self.quant_grad = flag
+
+    def forward(self, x):
+        w = quant_dequant_float(self.weight, self.w_qtype, True).to(x.dtype) if self.w_qtype else self.weight
+        xi = quant_dequant_float(x, self.in_qtype, True).to(x.dtype) if self.in_qtype else x
+        # straight-through: forward uses the rounded values, gradients pass unchanged
+        w = self.weight + (w - self.weight).detach()
+        xi = x + (xi - x).detach()
+        return F.linear(xi, w, self.bias)
+
+
+def replace_linear(module: nn.Module, w_Q, in_Q=None, quant_grad: bool = True, exclude_layers: List[str] = ()):
+    """Swap every ``nn.Linear`` of ``module`` for a :class:`QLinear` (utils/utils.py:16-40)."""
+    mods = dict(module.named_modules())
+    for n, m in list(module.named_modules()):
+        if n in exclude_layers or type(m) is not nn.Linear:
+            continue
+        q = QLinear(m.in_features, m.out_features, m.bias is not None).to(m.weight.device, m.weight.dtype)
+        q.transfer(m)
+        q.assign_qparams(w_Q)
+        q.set_quant_grad(quant_grad)
+        if in_Q is not None:
+            q.assign_input_qparams(in_Q)
+        parent = mods[".".join(n.split(".")[:-1])]
+        setattr(parent, n.split(".")[-1], q)
+    return module

@@ -61,7 +61,9 @@ def test_gemm_gated_residual(B, n, C, K, remap):
     else:
         y = ops.linear_gated_residual(x, w, b, resid.clone(), gate)
         r = ref.linear_gated_residual(x, w, b, resid, gate)
-    _close(y, r, 1e-3, 2e-2)
+    # y is rounded to bf16 before gating (as the reference's bf16 Linear output): one bf16
+    # ulp of |y| (≤ 2^-8·|y|) times |gate| may differ where fp32 sums straddle a rounding edge
+    _close(y, r, 1e-2, 6e-2)
     _no_device_error()
 
 
