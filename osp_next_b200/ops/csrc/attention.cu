@@ -10,13 +10,17 @@
 // CTA = 2 query tiles of 128 rows (one head, one segment, one batch entry).
 //   warp 0       TMA producer: Q0,Q1 once; then K_j, V_j into a 3-slot ring
 //   warp 1       MMA issuer:   S_t = Q_t·K_jᵀ (TMEM, fp32), O_t += P_t·V_j (TMEM, fp32)
-//   warps 2..5   softmax group 0 (tile 0), warps 6..9 softmax group 1 (tile 1):
+//   warps 4..7   softmax group 0 (tile 0), warps 8..11 softmax group 1 (tile 1):
 //                thread ↔ query row (warp w reads TMEM lanes 32·(w mod 4)…);
 //                S row from TMEM, online softmax in the exp2 domain with lazy O
 //                rescaling (only when the running max grows by more than 2^8),
 //                P written bf16 to 128B-swizzled smem; epilogue O/l → bf16, LSE.
 // The tensor core alternates tile 0 / tile 1 work so each softmax group overlaps
 // the other tile's MMAs.  TMEM: S0 | S1 | O0 | O1 (512 columns for D = 128).
+// Registers: launched at ≤168/thread (3 warps per SMSP); the producer/MMA
+// warpgroup then gives registers back (setmaxnreg.dec → 40) and the two softmax
+// warpgroups take them (setmaxnreg.inc → 200): 128·40 + 256·200 ≤ 384·168.
+// A quarter of the exponentials run on the FMA pipe (exp2_poly) instead of MUFU.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -29,7 +33,9 @@ namespace osp {
 constexpr int kQT = 128;      // rows per query tile
 constexpr int kKT = 128;      // keys per KV tile
 constexpr int kSlots = 3;     // K/V ring slots
-constexpr int kAttnThreads = 320;
+constexpr int kAttnThreads = 384;
+constexpr int kRegsLow = 40;          // producer / MMA warpgroup after setmaxnreg.dec
+constexpr int kRegsHigh = 200;        // softmax warpgroups after setmaxnreg.inc
 
 struct AttnArgs {
   const int* seg_q;
@@ -46,6 +52,24 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+
+// 2^x on the FMA pipe: Cody–Waite split x = n + f (n = ⌊x⌋, f ∈ [0,1)), a cubic
+// fitted to 2^f on [0,1] by iteratively reweighted least squares on Chebyshev
+// nodes (max relative error 7.5e-5, far below bf16's 3.9e-3), and 2^n added to the
+// exponent field.  Inputs below −126 flush to 0 (P entries that small vanish in bf16).
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -126.0f);
+  const float n = floorf(x);
+  const float f = x - n;
+  float p = fmaf(f, 0.07802443951368332f, 0.22606734931468964f);
+  p = fmaf(p, f, 0.6958334445953369f);
+  p = fmaf(p, f, 0.9999252557754517f);
+  const int e = __float2int_rn(n) << 23;
+  return __int_as_float(__float_as_int(p) + e);
+}
+
+__device__ __forceinline__ void regs_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" :: "n"(kRegsLow)); }
+__device__ __forceinline__ void regs_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" :: "n"(kRegsHigh)); }
 
 template <int D>
 struct AttnSmem {
@@ -118,7 +142,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
+  if (warp < 4) {
+  // producer / MMA warpgroup: hand registers to the softmax warpgroups
+  regs_dec();
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
     if (lane == 0) {
@@ -204,9 +230,11 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       umma_commit(done);
       mbar_wait(done, 0, args.err, kErrAttnTeardown);
     }
+  }
   } else {
-    // ------------------------------------------------------------------ softmax groups (warps 2..9)
-    const int t = (warp - 2) / 4;                  // query tile of this group
+    regs_inc();
+    // ------------------------------------------------------------------ softmax groups (warps 4..11)
+    const int t = (warp - 4) / 4;                  // query tile of this group
     const int quarter = warp & 3;                  // TMEM lane quarter this warp may access
     const int r = quarter * 32 + lane;             // row inside the tile
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
@@ -258,7 +286,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int c = c16 * 8 + i;
-          p[i] = (c < n_valid) ? ex2(fmaf(__uint_as_float(sr[c]), sl2, -m_ref)) : 0.f;
+          const float xe = fmaf(__uint_as_float(sr[c]), sl2, -m_ref);
+          p[i] = (c < n_valid) ? ((c16 & 3) == 3 ? exp2_poly(xe) : ex2(xe)) : 0.f;
           lsum += p[i];
         }
         uint4 w;
@@ -358,9 +387,17 @@ void attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   a.err = error_word(q.get_device());
   dim3 grid((unsigned)((max_q + 2 * kQT - 1) / (2 * kQT)), (unsigned)nseg, (unsigned)(B * H));
   auto stream = at::cuda::getCurrentCUDAStream();
+  // the setmaxnreg split must fit in what the launch allocates, or .inc would wait forever
+  auto check_regs = [](const void* fn) {
+    cudaFuncAttributes fa;
+    C10_CUDA_CHECK(cudaFuncGetAttributes(&fa, fn));
+    TORCH_CHECK(fa.numRegs * kAttnThreads >= 128 * kRegsLow + 256 * kRegsHigh,
+                "attention: register split exceeds launch allocation (numRegs=", fa.numRegs, ")");
+  };
   if (D == 128) {
     static bool cfg = false;
     if (!cfg) {
+      check_regs((const void*)attn_fwd_kernel<128>);
       C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           AttnSmem<128>::BYTES));
       cfg = true;
@@ -369,6 +406,7 @@ void attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   } else {
     static bool cfg = false;
     if (!cfg) {
+      check_regs((const void*)attn_fwd_kernel<64>);
       C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           AttnSmem<64>::BYTES));
       cfg = true;

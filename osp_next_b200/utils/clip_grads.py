@@ -36,7 +36,8 @@ def global_grad_norm(parameters, group=None) -> float:
     if grads:
         norms = torch._foreach_norm([g.float() for g in grads]) if dev.type == "cuda" else [g.float().norm() for g in grads]
         sq = torch.stack([n * n for n in norms]).sum()
-    if dist.is_initialized():
+    if group is not None and dist.is_initialized():
+        # shards are disjoint only inside the FSDP shard group (replicas hold copies)
         sq = sq.reshape(1)
         dist.all_reduce(sq, group=group)
     return float(sq.sqrt().item())
