@@ -514,3 +514,18 @@ models = {"osp_next": OSPNextModel}
 models_main_block = {"osp_next": OSPNextAttentionBlock}
 models_blocks_to_float = {"osp_next": [WanLayerNorm, WanRMSNorm]}
 models_blocks_to_output_float = {"osp_next": None}
+
+
+def _save_pretrained(self, path, **kw):
+    from .pretrained import save_pretrained
+    return save_pretrained(self, path, **kw)
+
+
+@classmethod
+def _from_pretrained(cls, path, **kw):
+    from .pretrained import from_pretrained
+    return from_pretrained(cls, path, **kw)
+
+
+OSPNextModel.save_pretrained = _save_pretrained
+OSPNextModel.from_pretrained = _from_pretrained

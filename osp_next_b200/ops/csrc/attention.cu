@@ -17,9 +17,9 @@
 //                P written bf16 to 128B-swizzled smem; epilogue O/l → bf16, LSE.
 // The tensor core alternates tile 0 / tile 1 work so each softmax group overlaps
 // the other tile's MMAs.  TMEM: S0 | S1 | O0 | O1 (512 columns for D = 128).
-// Registers: launched at ≤168/thread (3 warps per SMSP); the producer/MMA
-// warpgroup then gives registers back (setmaxnreg.dec → 40) and the two softmax
-// warpgroups take them (setmaxnreg.inc → 200): 128·40 + 256·200 ≤ 384·168.
+// Registers: ≤168/thread (3 warps per SMSP); the softmax reads S from TMEM twice
+// in 32-column chunks (max pass, then exp pass) so no 128-entry row is held in
+// registers.
 // A quarter of the exponentials run on the FMA pipe (exp2_poly) instead of MUFU.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -34,8 +34,6 @@ constexpr int kQT = 128;      // rows per query tile
 constexpr int kKT = 128;      // keys per KV tile
 constexpr int kSlots = 3;     // K/V ring slots
 constexpr int kAttnThreads = 384;
-constexpr int kRegsLow = 40;          // producer / MMA warpgroup after setmaxnreg.dec
-constexpr int kRegsHigh = 200;        // softmax warpgroups after setmaxnreg.inc
 
 struct AttnArgs {
   const int* seg_q;
@@ -67,9 +65,6 @@ __device__ __forceinline__ float exp2_poly(float x) {
   const int e = __float2int_rn(n) << 23;
   return __int_as_float(__float_as_int(p) + e);
 }
-
-__device__ __forceinline__ void regs_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" :: "n"(kRegsLow)); }
-__device__ __forceinline__ void regs_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" :: "n"(kRegsHigh)); }
 
 template <int D>
 struct AttnSmem {
@@ -143,8 +138,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (warp < 4) {
-  // producer / MMA warpgroup: hand registers to the softmax warpgroups
-  regs_dec();
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
     if (lane == 0) {
@@ -232,7 +225,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     }
   }
   } else {
-    regs_inc();
+
     // ------------------------------------------------------------------ softmax groups (warps 4..11)
     const int t = (warp - 4) / 4;                  // query tile of this group
     const int quarter = warp & 3;                  // TMEM lane quarter this warp may access
@@ -247,15 +240,18 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     for (int j = 0; j < n_kv; ++j) {
       if (!(ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, args.err, kErrAttnSoftmax)))) break;
       tc_fence_after();
-      uint32_t sr[kKT];
-#pragma unroll
-      for (int c = 0; c < kKT / 32; ++c) tmem_ld32(tSt + lane_off + c * 32, sr + c * 32);
-      tmem_ld_wait();
+      // pass 1: row max, 32 TMEM columns at a time (only 32 score registers live)
       const int n_valid = min(kKT, k_seg1 - k_seg0 - j * kKT);
       float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < kKT / 32; ++c) {
+        uint32_t sr[32];
+        tmem_ld32(tSt + lane_off + c * 32, sr);
+        tmem_ld_wait();
 #pragma unroll
-      for (int c = 0; c < kKT; ++c)
-        if (c < n_valid) mx = fmaxf(mx, __uint_as_float(sr[c]));
+        for (int i = 0; i < 32; ++i)
+          if (c * 32 + i < n_valid) mx = fmaxf(mx, __uint_as_float(sr[i]));
+      }
       mx *= sl2;
       const bool need = mx > m_ref + 8.0f;
       const float m_new = need ? mx : m_ref;
@@ -278,25 +274,33 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         }
       }
       m_ref = m_new;
-      // P = exp2(s·scale·log2e − m_ref) → bf16, 128B-swizzled K-major rows
+      // pass 2: P = exp2(s·scale·log2e − m_ref) → bf16, 128B-swizzled K-major rows;
+      // the S buffer stays valid until this group signals p_full
       float lsum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < kKT / 32; ++c) {
+        uint32_t sr[32];
+        tmem_ld32(tSt + lane_off + c * 32, sr);
+        tmem_ld_wait();
 #pragma unroll
-      for (int c16 = 0; c16 < kKT / 8; ++c16) {
-        float p[8];
+        for (int q8 = 0; q8 < 4; ++q8) {
+          const int c16 = c * 4 + q8;
+          float p[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int c = c16 * 8 + i;
-          const float xe = fmaf(__uint_as_float(sr[c]), sl2, -m_ref);
-          p[i] = (c < n_valid) ? ((c16 & 3) == 3 ? exp2_poly(xe) : ex2(xe)) : 0.f;
-          lsum += p[i];
+          for (int i = 0; i < 8; ++i) {
+            const int col = c16 * 8 + i;
+            const float xe = fmaf(__uint_as_float(sr[q8 * 8 + i]), sl2, -m_ref);
+            p[i] = (col < n_valid) ? (q8 == 3 ? exp2_poly(xe) : ex2(xe)) : 0.f;
+            lsum += p[i];
+          }
+          uint4 w;
+          w.x = pack_bf16x2(p[0], p[1]);
+          w.y = pack_bf16x2(p[2], p[3]);
+          w.z = pack_bf16x2(p[4], p[5]);
+          w.w = pack_bf16x2(p[6], p[7]);
+          const int box = c16 >> 3, chunk = c16 & 7;
+          *reinterpret_cast<uint4*>(pT + box * L::BOX + r * 128 + ((chunk ^ (r & 7)) << 4)) = w;
         }
-        uint4 w;
-        w.x = pack_bf16x2(p[0], p[1]);
-        w.y = pack_bf16x2(p[2], p[3]);
-        w.z = pack_bf16x2(p[4], p[5]);
-        w.w = pack_bf16x2(p[6], p[7]);
-        const int box = c16 >> 3, chunk = c16 & 7;
-        *reinterpret_cast<uint4*>(pT + box * L::BOX + r * 128 + ((chunk ^ (r & 7)) << 4)) = w;
       }
       l += lsum;
       fence_proxy_async_smem();
@@ -387,17 +391,9 @@ void attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   a.err = error_word(q.get_device());
   dim3 grid((unsigned)((max_q + 2 * kQT - 1) / (2 * kQT)), (unsigned)nseg, (unsigned)(B * H));
   auto stream = at::cuda::getCurrentCUDAStream();
-  // the setmaxnreg split must fit in what the launch allocates, or .inc would wait forever
-  auto check_regs = [](const void* fn) {
-    cudaFuncAttributes fa;
-    C10_CUDA_CHECK(cudaFuncGetAttributes(&fa, fn));
-    TORCH_CHECK(fa.numRegs * kAttnThreads >= 128 * kRegsLow + 256 * kRegsHigh,
-                "attention: register split exceeds launch allocation (numRegs=", fa.numRegs, ")");
-  };
   if (D == 128) {
     static bool cfg = false;
     if (!cfg) {
-      check_regs((const void*)attn_fwd_kernel<128>);
       C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           AttnSmem<128>::BYTES));
       cfg = true;
@@ -406,7 +402,6 @@ void attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   } else {
     static bool cfg = false;
     if (!cfg) {
-      check_regs((const void*)attn_fwd_kernel<64>);
       C10_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           AttnSmem<64>::BYTES));
       cfg = true;

@@ -26,6 +26,7 @@ void adamw(at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, dou
 void sde_step(const at::Tensor& x, const at::Tensor& v, const c10::optional<at::Tensor>& xi,
               const c10::optional<at::Tensor>& prev_in, at::Tensor& prev_out, const c10::optional<at::Tensor>& mean_out,
               at::Tensor& logp, double sigma, double dt, double smin, double smax);
+void wait_probe(int64_t mode, const at::Tensor& flag, double limit_s);
 
 static int* g_err[64] = {nullptr};
 static std::mutex g_err_mu;
@@ -64,5 +65,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("hif8_qdq", &osp::hif8_qdq);
   m.def("adamw", &osp::adamw);
   m.def("sde_step", &osp::sde_step);
+  m.def("wait_probe", &osp::wait_probe);
   m.def("get_error", &osp::get_error, pybind11::arg("device"), pybind11::arg("clear") = true);
 }

@@ -21,6 +21,7 @@ enum : int {
   kErrGemmProducer = 101, kErrGemmMma = 102, kErrGemmEpilogue = 103, kErrGemmTeardown = 104,
   kErrAttnProducer = 201, kErrAttnMma = 202, kErrAttnSoftmax = 203, kErrAttnTeardown = 204,
   kErrP2P = 301,
+  kErrProbeMbar = 901, kErrProbeFlag = 902,
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -60,17 +61,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait for phase `parity` of `bar`. False (and an error code) on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(addr, parity)) return true;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit_ns) {
       record_error(err, code);
       return false;
     }
   }
+}
+
+// Bounded wait until a global flag reaches `want` (peer signalling). False on timeout.
+__device__ __forceinline__ bool flag_wait(const volatile int* flag, int want, int* err, int code,
+                                          uint64_t limit_ns = kWaitLimitNs) {
+  const uint64_t t0 = globaltimer();
+  while (*flag < want) {
+    if (globaltimer() - t0 > limit_ns) {
+      record_error(err, code);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
 }
 
 // ------------------------------------------------------------------ TMA (tiled, no multicast)

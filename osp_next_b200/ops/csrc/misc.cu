@@ -251,3 +251,30 @@ void sde_step(const at::Tensor& x, const at::Tensor& v, const c10::optional<at::
 }
 
 }  // namespace osp
+
+namespace osp {
+// ------------------------------------------------------------------------------------ wait probes
+// Fault-handling self-test without a GPU fault: one CTA waits on an mbarrier phase
+// that nothing completes (mode 0) or on a global flag that nothing sets (mode 1),
+// with a short limit; the bounded wait records its error code and the kernel
+// returns normally, so the context stays usable.
+__global__ void wait_probe_kernel(int mode, const int* flag, unsigned long long limit_ns, int* err) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    if (mode == 0) {
+      mbar_init(&bar, 1);
+      fence_mbar_init();
+      mbar_wait(&bar, 0, err, kErrProbeMbar, limit_ns);
+    } else {
+      flag_wait(flag, 1, err, kErrProbeFlag, limit_ns);
+    }
+  }
+}
+
+void wait_probe(int64_t mode, const at::Tensor& flag, double limit_s) {
+  c10::cuda::CUDAGuard guard(flag.device());
+  wait_probe_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (int)mode, flag.data_ptr<int>(), (unsigned long long)(limit_s * 1e9), error_word(flag.get_device()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+}  // namespace osp

@@ -198,3 +198,16 @@ def test_sde_step_matches_reference():
                                prev_sample=prev)
     _close(mean, mean_ref, 1e-5, 1e-5)
     _close(lp, lp_ref, 1e-4, 1e-4)
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_bounded_wait_times_out_with_status(mode):
+    """A wait that can never complete (mbarrier phase / peer flag nobody sets) gives up
+    after its limit, reports its code through the error word, and the context stays usable."""
+    flag = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ops.ext().get_error(torch.cuda.current_device(), True)
+    ops.ext().wait_probe(mode, flag, 0.2)
+    code = ops.ext().get_error(torch.cuda.current_device(), True)
+    assert code == (901 if mode == 0 else 902)
+    x = torch.randn(256, 256, device=DEV).to(torch.bfloat16)
+    _close(ops.linear(x, x), ref.linear(x, x, out_dtype=torch.float32), 1e-2, 1e-1)

@@ -1,0 +1,4 @@
+#!/usr/bin/env bash
+# 8-GPU Mix-GRPO + LoRA (reference: scripts/train/gpu/train_osp_14b_RL.sh)
+torchrun --nnodes=${NNODES:-1} --nproc-per-node ${NPROC_PER_NODE:-8} --master-addr ${MASTER_ADDR:-127.0.0.1} \
+  --master-port ${MASTER_PORT:-29514} train/train_osp_RL.py --config ${CONFIG:-configs/train/osp_14b_RL.yaml}
