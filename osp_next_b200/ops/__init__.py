@@ -69,10 +69,23 @@ def linear(x, weight, bias=None, act: Optional[str] = None, out_dtype=_BF16):
     shp = x.shape
     a = _c(x.reshape(-1, shp[-1]).to(_BF16))
     w = _c(weight.to(_BF16))
+    N = w.shape[0]
+    # the kernel wants K % 8 == 0 (16-byte TMA rows) and N % 32 == 0: zero-pad otherwise
+    # (small LoRA ranks, odd token counts in weight gradients)
+    if a.shape[1] % 8:
+        pk = 8 - a.shape[1] % 8
+        a = torch.nn.functional.pad(a, (0, pk))
+        w = torch.nn.functional.pad(w, (0, pk))
+    b = None if bias is None else bias.float().contiguous()
+    if N % 32:
+        pn = 32 - N % 32
+        w = torch.nn.functional.pad(w, (0, 0, 0, pn))
+        b = None if b is None else torch.nn.functional.pad(b, (0, pn))
     out = torch.empty(a.shape[0], w.shape[0], dtype=out_dtype, device=x.device)
-    ext().gemm(a, w, None if bias is None else bias.float().contiguous(), out,
-               1 if act == "gelu_tanh" else 0, None, None, None, 0, 0)
-    return out.view(*shp[:-1], w.shape[0])
+    ext().gemm(a, w, b, out, 1 if act == "gelu_tanh" else 0, None, None, None, 0, 0)
+    if out.shape[1] != N:
+        out = out[:, :N].contiguous()
+    return out.view(*shp[:-1], N)
 
 
 def linear_gated_residual(x, weight, bias, resid, gate=None, dest_row=None, n_out=None, out=None):
