@@ -81,6 +81,7 @@ class BlockContext:
     ulysses_group: object = None      # process group for the head all-to-all (None: none)
     next_dest_row: Optional[torch.Tensor] = None   # fuse the layout change into FFN-down (1 GPU)
     next_n: int = 0
+    relaid: bool = False              # set when the block stored its output in the next layout
 
 
 class OSPNextSelfAttention(nn.Module):
@@ -239,6 +240,7 @@ class OSPNextAttentionBlock(nn.Module):
             h = self.ffn[1](f0(xm))
         if _plain(f2) and ctx.next_dest_row is not None and Fn._fused(h, f2.weight, x):
             # layout change for the next block fused into the FFN-down store
+            ctx.relaid = True
             return Fn.ops.linear_gated_residual(h, f2.weight, f2.bias, x, e[5],
                                                 dest_row=ctx.next_dest_row, n_out=ctx.next_n)
         if _plain(f2):
@@ -458,7 +460,7 @@ class OSPNextModel(nn.Module):
                     kv = block.cross_attn.text_kv(text)
                     self._text_kv_cache[key] = kv
             x = block(x, e0, text, ctx, kv, gradient_checkpointing=self.gradient_checkpointing)
-            if fuse:
+            if ctx.relaid:                   # the FFN-down epilogue already stored the next layout
                 prev_kind = nxt
         x = self.head(x, e)
         # back to natural order, full sequence on every rank
