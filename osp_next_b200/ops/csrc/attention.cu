@@ -17,9 +17,9 @@
 //                P written bf16 to 128B-swizzled smem; epilogue O/l → bf16, LSE.
 // The tensor core alternates tile 0 / tile 1 work so each softmax group overlaps
 // the other tile's MMAs.  TMEM: S0 | S1 | O0 | O1 (512 columns for D = 128).
-// Registers: ≤168/thread (3 warps per SMSP); the softmax reads S from TMEM twice
-// in 32-column chunks (max pass, then exp pass) so no 128-entry row is held in
-// registers.
+// Softmax: one S row (128 fp32) per thread from four TMEM loads and one wait;
+// full KV tiles skip the per-column key mask; 3-input max, packed f32x2 FMA/ADD
+// (sm_100a) for the scale/shift, the row sum and the FMA-pipe exponentials.
 // A quarter of the exponentials run on the FMA pipe (exp2_poly) instead of MUFU.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -64,6 +64,47 @@ __device__ __forceinline__ float exp2_poly(float x) {
   p = fmaf(p, f, 0.9999252557754517f);
   const int e = __float2int_rn(n) << 23;
   return __int_as_float(__float_as_int(p) + e);
+}
+
+// Packed fp32x2 helpers (sm_100a FFMA2 / FADD2): two lanes of math per instruction.
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// exp2 of a pair on the FMA pipe (same method as exp2_poly, polynomial in f32x2)
+__device__ __forceinline__ uint64_t exp2_poly2(float x0, float x1) {
+  x0 = fmaxf(x0, -126.0f);
+  x1 = fmaxf(x1, -126.0f);
+  const float n0 = floorf(x0), n1 = floorf(x1);
+  const uint64_t f = fadd2(pk2(x0, x1), pk2(-n0, -n1));
+  uint64_t p = ffma2(f, pk2(0.07802443951368332f, 0.07802443951368332f),
+                     pk2(0.22606734931468964f, 0.22606734931468964f));
+  p = ffma2(p, f, pk2(0.6958334445953369f, 0.6958334445953369f));
+  p = ffma2(p, f, pk2(0.9999252557754517f, 0.9999252557754517f));
+  float p0, p1;
+  upk2(p, p0, p1);
+  p0 = __int_as_float(__float_as_int(p0) + (__float2int_rn(n0) << 23));
+  p1 = __int_as_float(__float_as_int(p1) + (__float2int_rn(n1) << 23));
+  return pk2(p0, p1);
 }
 
 template <int D>
@@ -240,17 +281,27 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     for (int j = 0; j < n_kv; ++j) {
       if (!(ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, args.err, kErrAttnSoftmax)))) break;
       tc_fence_after();
-      // pass 1: row max, 32 TMEM columns at a time (only 32 score registers live)
+      // S row → registers (four 32-column TMEM loads, one wait)
       const int n_valid = min(kKT, k_seg1 - k_seg0 - j * kKT);
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < kKT / 32; ++c) {
-        uint32_t sr[32];
-        tmem_ld32(tSt + lane_off + c * 32, sr);
-        tmem_ld_wait();
+      const bool full_tile = n_valid == kKT;
+      uint32_t sr[kKT];
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c * 32 + i < n_valid) mx = fmaxf(mx, __uint_as_float(sr[i]));
+      for (int c = 0; c < kKT / 32; ++c) tmem_ld32(tSt + lane_off + c * 32, sr + c * 32);
+      tmem_ld_wait();
+      float mx;
+      if (full_tile) {
+        float m2[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < kKT; c += 4) {
+          m2[0] = max3(m2[0], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+          m2[1] = max3(m2[1], __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+        }
+        mx = fmaxf(m2[0], m2[1]);
+      } else {
+        mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < kKT; ++c)
+          if (c < n_valid) mx = fmaxf(mx, __uint_as_float(sr[c]));
       }
       mx *= sl2;
       const bool need = mx > m_ref + 8.0f;
@@ -274,34 +325,44 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         }
       }
       m_ref = m_new;
-      // pass 2: P = exp2(s·scale·log2e − m_ref) → bf16, 128B-swizzled K-major rows;
-      // the S buffer stays valid until this group signals p_full
-      float lsum = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < kKT / 32; ++c) {
-        uint32_t sr[32];
-        tmem_ld32(tSt + lane_off + c * 32, sr);
-        tmem_ld_wait();
+      // P = exp2(s·scale·log2e − m_ref) → bf16, 128B-swizzled K-major rows.  Scale/shift and
+      // the row sum run as packed f32x2; every fourth 8-column group uses the FMA-pipe exp2.
+      const uint64_t sl2x2 = pk2(sl2, sl2), negm2 = pk2(-m_ref, -m_ref);
+      uint64_t ls2 = pk2(0.f, 0.f);
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          const int c16 = c * 4 + q8;
-          float p[8];
+      for (int c16 = 0; c16 < kKT / 8; ++c16) {
+        uint64_t pp[4];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int col = c16 * 8 + i;
-            const float xe = fmaf(__uint_as_float(sr[q8 * 8 + i]), sl2, -m_ref);
-            p[i] = (col < n_valid) ? (q8 == 3 ? exp2_poly(xe) : ex2(xe)) : 0.f;
-            lsum += p[i];
+        for (int i = 0; i < 4; ++i) {
+          const int c = c16 * 8 + 2 * i;
+          const uint64_t xe = ffma2(pk2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sl2x2, negm2);
+          float x0, x1;
+          upk2(xe, x0, x1);
+          uint64_t e;
+          if ((c16 & 3) == 3) e = exp2_poly2(x0, x1);
+          else e = pk2(ex2(x0), ex2(x1));
+          if (!full_tile) {
+            float e0, e1;
+            upk2(e, e0, e1);
+            e = pk2(c < n_valid ? e0 : 0.f, c + 1 < n_valid ? e1 : 0.f);
           }
-          uint4 w;
-          w.x = pack_bf16x2(p[0], p[1]);
-          w.y = pack_bf16x2(p[2], p[3]);
-          w.z = pack_bf16x2(p[4], p[5]);
-          w.w = pack_bf16x2(p[6], p[7]);
-          const int box = c16 >> 3, chunk = c16 & 7;
-          *reinterpret_cast<uint4*>(pT + box * L::BOX + r * 128 + ((chunk ^ (r & 7)) << 4)) = w;
+          pp[i] = e;
+          ls2 = fadd2(ls2, e);
         }
+        float p[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) upk2(pp[i], p[2 * i], p[2 * i + 1]);
+        uint4 w;
+        w.x = pack_bf16x2(p[0], p[1]);
+        w.y = pack_bf16x2(p[2], p[3]);
+        w.z = pack_bf16x2(p[4], p[5]);
+        w.w = pack_bf16x2(p[6], p[7]);
+        const int box = c16 >> 3, chunk = c16 & 7;
+        *reinterpret_cast<uint4*>(pT + box * L::BOX + r * 128 + ((chunk ^ (r & 7)) << 4)) = w;
       }
+      float ls_a, ls_b;
+      upk2(ls2, ls_a, ls_b);
+      const float lsum = ls_a + ls_b;
       l += lsum;
       fence_proxy_async_smem();
       tc_fence_before();

@@ -211,3 +211,39 @@ def test_bounded_wait_times_out_with_status(mode):
     assert code == (901 if mode == 0 else 902)
     x = torch.randn(256, 256, device=DEV).to(torch.bfloat16)
     _close(ops.linear(x, x), ref.linear(x, x, out_dtype=torch.float32), 1e-2, 1e-1)
+
+
+@pytest.mark.parametrize("M,N,K", [(100, 8, 64), (77, 40, 12), (50, 64, 8)])
+def test_gemm_padded_shapes(M, N, K):
+    """Shapes outside the kernel's native tiling (small LoRA ranks, odd K) are zero-padded."""
+    torch.manual_seed(10)
+    x = torch.randn(M, K, device=DEV).to(torch.bfloat16)
+    w = torch.randn(N, K, device=DEV).to(torch.bfloat16)
+    b = torch.randn(N, device=DEV)
+    _close(ops.linear(x, w, b, out_dtype=torch.float32), ref.linear(x, w, b, out_dtype=torch.float32), 1e-4, 1e-3)
+
+
+def test_model_fused_path_matches_autograd_path_with_wrapped_ffn():
+    """Inference (fused kernels, fused layout-change stores) and training (autograd) paths
+    agree, also when FFN-down is a wrapped Linear (LoRA) that cannot take the fused store."""
+    from osp_next_b200.models.lora import LoraModel
+    from osp_next_b200.models.osp_next import OSPNextModel
+    torch.manual_seed(0)
+    with torch.device(DEV):
+        m = OSPNextModel(dim=256, ffn_dim=512, num_heads=2, num_layers=4, text_len=16,
+                         skiparse_model_type="dual_end", sparse_ratio=2, num_full_blocks=0)
+    for targets in (None, ["ffn.2", "self_attn.q"]):
+        net = m if targets is None else LoraModel(m, r=8, lora_alpha=8, target_modules=targets)
+        if targets is not None:
+            for mod in net.lora_modules():
+                torch.nn.init.normal_(mod.lora_B["default"].weight, std=0.02)
+        x = torch.randn(1, 16, 3, 16, 16, device=DEV)
+        t = torch.tensor([400.0], device=DEV)
+        ctx = torch.randn(1, 16, 4096, device=DEV)
+        net.eval()
+        with torch.no_grad():
+            a = net(x, t, ctx)
+        net.train()
+        b = net(x, t, ctx)
+        rel = (a - b.detach()).norm() / b.detach().norm()
+        assert rel < 2e-2, rel
