@@ -63,6 +63,8 @@ def parse():
     p.add_argument("--guidance", type=float, default=5.0)
     p.add_argument("--shift", type=float, default=5.0)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                   help="SSP layout exchange: fused GEMM-epilogue stores over NVLink, or NCCL all_to_all")
     return p.parse_args()
 
 
@@ -193,6 +195,10 @@ def run_ours(args, rank, world, local):
         attach_sp(model, rt)
         from osp_next_b200.parallel.sp_state import sp_state
         cfg_par = CFGParallel(sp_state.cfg_group) if cfg_size > 1 else None
+        if ssp > 1 and args.exchange == "p2p":
+            from osp_next_b200.parallel.sp import enable_p2p_exchange
+            _, _, T, Hl, Wl = latent_shape(args)
+            enable_p2p_exchange(model, 1, (T, Hl // 2, Wl // 2), dev)
     sched = FlowMatchingScheduler(num_inference_steps=STEPS_PER_VIDEO, guidance_scale=args.guidance,
                                   shift=args.shift)
     shape = latent_shape(args)
@@ -242,6 +248,8 @@ def run_ours(args, rank, world, local):
                "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": d2h // args.steps,
                "note": "public T2VInferencePipeline call; inputs from pinned host, latent read back"}
     err = ops.ext().get_error(local, True)
+    if getattr(getattr(model, "parallel", None), "p2p", None) is not None:
+        model.parallel.p2p.close()
     return ms, launches, clocks, e2e, {"finite": finite, "device_error": err}
 
 
@@ -302,6 +310,8 @@ def main():
     rank, world, local = init_dist(args.gpus)
     cfg_size, ssp = layout_for(world)
     par = {1: "single", 2: "cfg2", 4: "cfg2_ssp2", 8: "cfg2_ssp4"}[world]
+    if world >= 4 and args.impl == "ours":
+        par += "_" + args.exchange
     base = {"metric": "sec/video OSP-Next-14B 81f 720P(padded 768x1280) 50-step CFG5 T2V",
             "unit": "s/video", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": False, "scaling": "strong", "dtype": "bf16",

@@ -82,6 +82,7 @@ class BlockContext:
     next_dest_row: Optional[torch.Tensor] = None   # fuse the layout change into FFN-down (1 GPU)
     next_n: int = 0
     relaid: bool = False              # set when the block stored its output in the next layout
+    p2p: Optional[tuple] = None       # (peer pointer table, dest_rank, dest_row, n_stride): fused SSP exchange
 
 
 class OSPNextSelfAttention(nn.Module):
@@ -238,6 +239,12 @@ class OSPNextAttentionBlock(nn.Module):
             h = Fn.linear(xm, f0.weight, f0.bias, act="gelu_tanh")
         else:
             h = self.ffn[1](f0(xm))
+        if _plain(f2) and ctx.p2p is not None and Fn._fused(h, f2.weight, x):
+            # fused SSP exchange: every output row goes straight to its owner rank over NVLink
+            ptrs, drank, drow, stride = ctx.p2p
+            Fn.ops.linear_gated_residual_p2p(h, f2.weight, f2.bias, x, e[5], drank, drow, ptrs, stride)
+            ctx.relaid = True
+            return None
         if _plain(f2) and ctx.next_dest_row is not None and Fn._fused(h, f2.weight, x):
             # layout change for the next block fused into the FFN-down store
             ctx.relaid = True
@@ -452,6 +459,13 @@ class OSPNextModel(nn.Module):
                 rd = make_redistribution(kind, nxt, grid, P, spec)
                 ctx.next_dest_row = _dev(rd.dest_row, device, torch.int32)
                 ctx.next_n = rd.n_out
+            p2p = getattr(rt, "p2p", None) if rt is not None else None
+            use_p2p = (p2p is not None and spec.world > 1 and spec.full_sp == spec.world and nxt is not None
+                       and nxt != kind and x.is_cuda and not torch.is_grad_enabled())
+            if use_p2p:
+                rd = make_redistribution(kind, nxt, grid, P, spec)
+                ctx.p2p = (p2p.target(), _dev(rd.dest_rank, device, torch.int32),
+                           _dev(rd.dest_row, device, torch.int32), p2p.n_stride)
             kv = None
             if self._text_kv_cache is not None and not torch.is_grad_enabled():
                 key = (i, text.data_ptr(), text.shape)
@@ -461,6 +475,9 @@ class OSPNextModel(nn.Module):
                     self._text_kv_cache[key] = kv
             x = block(x, e0, text, ctx, kv, gradient_checkpointing=self.gradient_checkpointing)
             if ctx.relaid:                   # the FFN-down epilogue already stored the next layout
+                if ctx.p2p is not None:      # peers wrote into our buffer: order, then read it
+                    p2p.barrier()
+                    x = p2p.take(rd.n_out)
                 prev_kind = nxt
         x = self.head(x, e)
         # back to natural order, full sequence on every rank

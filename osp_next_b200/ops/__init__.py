@@ -116,6 +116,19 @@ def linear_gated_residual(x, weight, bias, resid, gate=None, dest_row=None, n_ou
     return out
 
 
+def linear_gated_residual_p2p(x, weight, bias, resid, gate, dest_rank, dest_row, out_ptrs, n_stride: int):
+    """Fused SSP exchange: row m of every batch entry b of ``resid + (x·Wᵀ+b)·gate`` is
+    stored at row ``b·n_stride + dest_row[m]`` of rank ``dest_rank[m]``'s buffer
+    (``out_ptrs`` = device int64 table of the peers' buffer base pointers)."""
+    B, n, K = x.shape
+    a = _c(x.reshape(B * n, K).to(_BF16))
+    w = _c(weight.to(_BF16))
+    C = w.shape[0]
+    ext().gemm_p2p(a, w, None if bias is None else bias.float().contiguous(), _c(resid.float()).view(-1, C),
+                   None if gate is None else gate.float().contiguous(), dest_rank, dest_row, out_ptrs, n,
+                   int(n_stride))
+
+
 # ----------------------------------------------------------------------------- attention
 
 def qk_norm_rope(qkv, wq, wk, pos, freqs, num_heads: int, eps: float = 1e-6):

@@ -27,6 +27,15 @@ void sde_step(const at::Tensor& x, const at::Tensor& v, const c10::optional<at::
               const c10::optional<at::Tensor>& prev_in, at::Tensor& prev_out, const c10::optional<at::Tensor>& mean_out,
               at::Tensor& logp, double sigma, double dt, double smin, double smax);
 void wait_probe(int64_t mode, const at::Tensor& flag, double limit_s);
+void gemm_p2p(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& bias,
+              const at::Tensor& resid, const c10::optional<at::Tensor>& gate, const at::Tensor& dest_rank,
+              const at::Tensor& dest_row, const at::Tensor& out_ptrs, int64_t rows_per_batch, int64_t n_stride);
+std::tuple<int64_t, std::string> p2p_alloc(int64_t bytes);
+int64_t p2p_open(const std::string& handle);
+void p2p_close(int64_t ptr);
+void p2p_free(int64_t ptr);
+at::Tensor p2p_view(int64_t ptr, std::vector<int64_t> shape, at::ScalarType dtype, int64_t device);
+void p2p_barrier(const at::Tensor& flag_ptrs, int64_t rank, int64_t world, int64_t epoch, double limit_s);
 
 static int* g_err[64] = {nullptr};
 static std::mutex g_err_mu;
@@ -66,5 +75,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw", &osp::adamw);
   m.def("sde_step", &osp::sde_step);
   m.def("wait_probe", &osp::wait_probe);
+  m.def("gemm_p2p", &osp::gemm_p2p);
+  m.def("p2p_alloc", [](int64_t bytes) {
+    auto r = osp::p2p_alloc(bytes);
+    return pybind11::make_tuple(std::get<0>(r), pybind11::bytes(std::get<1>(r)));
+  });
+  m.def("p2p_open", [](pybind11::bytes h) { return osp::p2p_open(std::string(h)); });
+  m.def("p2p_close", &osp::p2p_close);
+  m.def("p2p_free", &osp::p2p_free);
+  m.def("p2p_view", &osp::p2p_view);
+  m.def("p2p_barrier", &osp::p2p_barrier);
   m.def("get_error", &osp::get_error, pybind11::arg("device"), pybind11::arg("clear") = true);
 }

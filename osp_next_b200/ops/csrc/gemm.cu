@@ -40,6 +40,8 @@ struct GemmArgs {
   const int* dest_row;      // [rows_per_batch] or null
   int rows_per_batch;       // n (residual mode)
   int n_out;                // rows per batch of out (residual mode with dest_row)
+  const int64_t* out_ptrs;  // [world] peer output buffers (fused SSP exchange) or null
+  const int* dest_rank;     // [rows_per_batch] owner rank of each row in the next layout
   int* err;
 };
 
@@ -176,11 +178,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       const bool row_ok = row < args.M;
       long out_row = row;
       int bidx = 0;
+      float* out_base = reinterpret_cast<float*>(args.out);
       if (MODE == kEpiResidual && row_ok) {
         bidx = row / args.rows_per_batch;
         if (args.dest_row) {
           const int m = row - bidx * args.rows_per_batch;
           out_row = (long)bidx * args.n_out + args.dest_row[m];
+          // fused SSP exchange: the row is stored into the owner's buffer over NVLink
+          if (args.out_ptrs) out_base = reinterpret_cast<float*>(args.out_ptrs[args.dest_rank[m]]);
         }
       }
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
@@ -227,7 +232,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         } else {
           // resid + bf16(y)·gate  (the Linear output is bf16 under autocast in the reference)
           const float4* r4 = reinterpret_cast<const float4*>(args.resid + (long)row * args.N + col0);
-          float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + out_row * args.N + col0);
+          float4* o4 = reinterpret_cast<float4*>(out_base + out_row * args.N + col0);
           const float4* g4 = args.gate ? reinterpret_cast<const float4*>(args.gate + (long)bidx * args.N + col0)
                                        : nullptr;
 #pragma unroll
@@ -354,6 +359,42 @@ void gemm(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tens
     else if (args.N % 128 == 0) launch_gemm<128, kEpiStore, float>(a, b, args, stream);
     else launch_gemm<64, kEpiStore, float>(a, b, args, stream);
   }
+}
+
+// Fused SSP exchange: out_ptrs[dest_rank[m]][b·n_stride + dest_row[m]] = resid[b,m] + (a·bᵀ + bias)·gate[b]
+void gemm_p2p(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& bias,
+              const at::Tensor& resid, const c10::optional<at::Tensor>& gate, const at::Tensor& dest_rank,
+              const at::Tensor& dest_row, const at::Tensor& out_ptrs, int64_t rows_per_batch, int64_t n_stride) {
+  TORCH_CHECK(a.is_cuda() && a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 &&
+              a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1) && a.stride(1) == 1 && b.stride(1) == 1,
+              "gemm_p2p: bf16 K-contiguous operands");
+  TORCH_CHECK(a.size(1) % 8 == 0 && b.size(0) % 32 == 0, "gemm_p2p: K % 8 == 0, N % 32 == 0");
+  TORCH_CHECK(resid.scalar_type() == at::kFloat && resid.is_contiguous(), "gemm_p2p: fp32 residual");
+  TORCH_CHECK(dest_rank.scalar_type() == at::kInt && dest_row.scalar_type() == at::kInt &&
+              dest_rank.numel() == rows_per_batch && dest_row.numel() == rows_per_batch, "gemm_p2p: int32 maps [n]");
+  TORCH_CHECK(out_ptrs.scalar_type() == at::kLong && out_ptrs.is_cuda(), "gemm_p2p: int64 device pointer table");
+  c10::cuda::CUDAGuard guard(a.device());
+  GemmArgs args{};
+  args.M = (int)a.size(0);
+  args.N = (int)b.size(0);
+  args.K = (int)a.size(1);
+  TORCH_CHECK(resid.numel() == (int64_t)args.M * args.N && args.M % rows_per_batch == 0, "gemm_p2p: shapes");
+  args.bias = bias.has_value() ? bias->data_ptr<float>() : nullptr;
+  args.act = 0;
+  args.out = nullptr;
+  args.resid = resid.data_ptr<float>();
+  args.gate = gate.has_value() ? gate->data_ptr<float>() : nullptr;
+  args.dest_row = dest_row.data_ptr<int>();
+  args.dest_rank = dest_rank.data_ptr<int>();
+  args.out_ptrs = out_ptrs.data_ptr<int64_t>();
+  args.rows_per_batch = (int)rows_per_batch;
+  args.n_out = (int)n_stride;
+  args.err = error_word(a.get_device());
+  if (args.M == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (args.N % 256 == 0) launch_gemm<256, kEpiResidual, float>(a, b, args, stream);
+  else if (args.N % 128 == 0) launch_gemm<128, kEpiResidual, float>(a, b, args, stream);
+  else launch_gemm<64, kEpiResidual, float>(a, b, args, stream);
 }
 
 }  // namespace osp

@@ -25,6 +25,7 @@ class SPRuntime:
     ulysses_group: object = None
     full_group: object = None
     skiparse_group: object = None
+    p2p: object = None            # parallel.p2p.P2PExchange when the fused NVLink exchange is on
 
 
 def _new_groups(world: int, size: int, stride: int = 1, block: int = None):
@@ -77,3 +78,24 @@ def attach_sp(model, runtime: Optional[SPRuntime]):
         target = base.model
     target.parallel = runtime if (runtime is not None and runtime.spec.world > 1) else None
     return model
+
+
+def enable_p2p_exchange(model, batch: int, grid, device):
+    """Turn on the fused NVLink SSP exchange for a model whose SP runtime is attached.
+
+    Buffers are sized for the largest per-rank row count over the model's layouts
+    (one common row stride), for ``batch`` samples of ``grid`` patches.
+    """
+    from ..models.layout import ParallelSpec, make_layout
+    from .p2p import P2PExchange
+    rt = getattr(model, "parallel", None)
+    if rt is None or rt.spec.world == 1 or rt.spec.full_sp != rt.spec.world:
+        return None
+    P = model.sparse_ratio
+    n_stride = 0
+    for kind in set(model.block_kinds):
+        for r in range(rt.spec.world):
+            sp = ParallelSpec(rt.spec.ssp, rt.spec.ulysses, rt.spec.full_sp, r)
+            n_stride = max(n_stride, make_layout(kind, tuple(grid), P, sp).n_local)
+    rt.p2p = P2PExchange(rt.global_sp_group, batch, n_stride, model.dim, device)
+    return rt.p2p

@@ -1,0 +1,89 @@
+"""Multi-GPU sequence parallelism on NCCL vs one GPU (skipped with fewer than 2 GPUs).
+
+Ranks are separate processes, one per GPU; NVLS is disabled (NCCL_NVLS_ENABLE=0) and a
+short process-group timeout bounds every collective.
+"""
+import os
+import socket
+import tempfile
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+CFG = dict(dim=256, ffn_dim=512, num_heads=4, num_layers=8, text_len=16, skiparse_model_type="dual_end",
+           sparse_ratio=2, num_full_blocks=4)
+SHAPE = (1, 16, 3, 24, 32)
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _build(device):
+    from osp_next_b200.models.osp_next import OSPNextModel
+    torch.manual_seed(0)
+    with torch.device(device):
+        m = OSPNextModel(**CFG)
+    return m.to(torch.bfloat16).eval()
+
+
+def _inputs(device):
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(*SHAPE, generator=g).to(device, torch.bfloat16)
+    t = torch.tensor([500.0], device=device)
+    ctx = torch.randn(1, CFG["text_len"], 4096, generator=g).to(device, torch.bfloat16)
+    return x, t, ctx
+
+
+def _worker(rank, world, port, ssp, exchange, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    from osp_next_b200.parallel.sp import attach_sp, build_sp_groups
+    dev = torch.device("cuda", rank)
+    m = _build(dev)
+    attach_sp(m, build_sp_groups(CFG["num_heads"], skiparse_sp_size=ssp, sp_size=1))
+    if exchange == "p2p":
+        from osp_next_b200.parallel.sp import enable_p2p_exchange
+        enable_p2p_exchange(m, SHAPE[0], (SHAPE[2], SHAPE[3] // 2, SHAPE[4] // 2), dev)
+    x, t, ctx = _inputs(dev)
+    with torch.no_grad():
+        y = m(x, t, ctx)
+    from osp_next_b200 import ops
+    torch.save({"y": y.float().cpu(), "err": ops.ext().get_error(rank, True)}, os.path.join(out_dir, f"r{rank}.pt"))
+    if m.parallel is not None and m.parallel.p2p is not None:
+        m.parallel.p2p.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
+@pytest.mark.parametrize("ssp", [2, 4])
+def test_ssp_matches_single_gpu(ssp, exchange):
+    if torch.cuda.device_count() < ssp:
+        pytest.skip(f"needs {ssp} GPUs")
+    m = _build("cuda:0")
+    x, t, ctx = _inputs("cuda:0")
+    with torch.no_grad():
+        y1 = m(x, t, ctx).float().cpu()
+    del m
+    torch.cuda.empty_cache()
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_worker, args=(ssp, _port(), ssp, exchange, d), nprocs=ssp, join=True,
+                           start_method="spawn")
+        for r in range(ssp):
+            o = torch.load(os.path.join(d, f"r{r}.pt"))
+            assert o["err"] == 0
+            rel = (o["y"] - y1).norm() / y1.norm()
+            assert rel < 2e-2, (r, rel)
