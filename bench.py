@@ -187,7 +187,7 @@ def run_ours(args, rank, world, local):
     for n_, p in model.named_parameters():
         if "norm" in n_ or "modulation" in n_:
             p.data = p.data.float()
-    model.enable_text_kv_cache(True)
+    # no text K/V cache: every timed step recomputes the cross-attention K/V like the reference
     cfg_size, ssp = layout_for(world)
     cfg_par = None
     if world > 1:

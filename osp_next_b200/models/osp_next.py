@@ -387,8 +387,16 @@ class OSPNextModel(nn.Module):
         return self._freqs
 
     def enable_text_kv_cache(self, enabled: bool = True):
-        """Cache cross-attention K/V of the text per block (constant across sampler steps)."""
+        """Cache cross-attention K/V of the text per block (constant across sampler steps).
+
+        Entries are keyed by the text tensor's storage; the sampler clears the cache at
+        the start of every ``sample`` call so a reused allocation never serves stale K/V.
+        """
         self._text_kv_cache = {} if enabled else None
+
+    def reset_text_kv_cache(self):
+        if self._text_kv_cache is not None:
+            self._text_kv_cache.clear()
 
     # ------------------------------------------------------------------ embeddings
     def patchify_embed(self, x):

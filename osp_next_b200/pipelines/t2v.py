@@ -87,7 +87,8 @@ class T2VInferencePipeline:
     @torch.inference_mode()
     def __call__(self, prompt=None, negative_prompt=None, prompt_embeds=None, negative_prompt_embeds=None,
                  num_frames=49, height=480, width=832, seed=None, max_sequence_length=512, device="cuda:0",
-                 latents=None, output_type: str = "video", cfg_parallel=None, max_steps: Optional[int] = None):
+                 latents=None, output_type: str = "video", cfg_parallel=None, max_steps: Optional[int] = None,
+                 cuda_graph: bool = False):
         if negative_prompt is None or negative_prompt == "":
             negative_prompt = NEGATIVE_PROMPT
         batch_size = 1 if isinstance(prompt, str) else (len(prompt) if prompt is not None else prompt_embeds.shape[0])
@@ -107,7 +108,7 @@ class T2VInferencePipeline:
         latents = self.prepare_latents(shape, generator, device, prompt_embeds.dtype, latents)
         latents = self.scheduler.sample(self.predictor, latents, prompt_embeds=prompt_embeds,
                                         negative_prompt_embeds=negative_prompt_embeds, cfg_parallel=cfg_parallel,
-                                        max_steps=max_steps)
+                                        max_steps=max_steps, cuda_graph=cuda_graph)
         if output_type == "latent" or self.vae is None:
             return latents
         return self.decode_latents(latents.to(self.vae.dtype))

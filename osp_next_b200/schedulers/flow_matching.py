@@ -109,18 +109,31 @@ class FlowMatchingScheduler:
         return latents, latents
 
     def sample(self, model, latents, prompt_embeds=None, negative_prompt_embeds=None,
-               step_callback: Optional[Callable] = None, cfg_parallel=None, max_steps=None, **model_kwargs):
+               step_callback: Optional[Callable] = None, cfg_parallel=None, max_steps=None,
+               cuda_graph: bool = False, **model_kwargs):
         """Euler sampling with CFG.
 
         ``cfg_parallel``: optional :class:`osp_next_b200.parallel.cfg.CFGParallel`
         that runs cond on one half of the ranks and uncond on the other.
         ``max_steps``: stop after the first steps of the schedule (timing runs).
+        ``cuda_graph``: capture the model call once (after one eager warm-up step) and
+        replay it for the remaining steps; single-GPU CUDA inference only.
         """
         n = self.num_inference_steps
         sigmas = self._set_sigmas(training=False)
         timesteps = sigmas.clone() * 1000
         cfg = self.do_classifier_free_guidance and negative_prompt_embeds is not None
         g = self.guidance_scale
+        if hasattr(model, "reset_text_kv_cache"):
+            model.reset_text_kv_cache()
+        graphed = bool(cuda_graph and latents.is_cuda and getattr(model, "parallel", None) is None
+                       and cfg_parallel is None)
+        if graphed:
+            from ..utils.graphs import CUDAGraphRunner
+            model = CUDAGraphRunner(model)
+        e2 = None
+        if cfg and cfg_parallel is None and self.batch_cfg:
+            e2 = torch.cat([prompt_embeds, negative_prompt_embeds], 0)
         for i in range(n if max_steps is None else min(n, max_steps)):
             t = timesteps[i]
             dt_sigma = float(sigmas[i + 1] - sigmas[i])
@@ -132,11 +145,12 @@ class FlowMatchingScheduler:
                 latents = ops.cfg_euler_step(latents, cond, uncond, g, dt_sigma)
             elif cfg and self.batch_cfg:
                 x2 = torch.cat([latents, latents], 0)
-                e2 = torch.cat([prompt_embeds, negative_prompt_embeds], 0)
                 pred = model(x2, t.expand(2 * B).to(latents.device), e2)
                 latents = ops.cfg_euler_step(latents, pred[:B], pred[B:], g, dt_sigma)
             elif cfg:
                 cond = model(latents, t.expand(B).to(latents.device), prompt_embeds)
+                if graphed:                  # the next replay overwrites the static output
+                    cond = cond.clone()
                 uncond = model(latents, t.expand(B).to(latents.device), negative_prompt_embeds)
                 latents = ops.cfg_euler_step(latents, cond, uncond, g, dt_sigma)
             else:
