@@ -20,6 +20,7 @@ What differs from the reference is *how* a block runs (the math is the same):
 """
 from __future__ import annotations
 
+import functools
 import math
 from dataclasses import dataclass
 from typing import List, Optional, Tuple
@@ -41,7 +42,8 @@ def sinusoidal_embedding_1d(dim: int, position: torch.Tensor) -> torch.Tensor:
     assert dim % 2 == 0
     half = dim // 2
     position = position.type(torch.float64)
-    sinusoid = torch.outer(position, torch.pow(10000, -torch.arange(half).to(position).div(half)))
+    idx = torch.arange(half, device=position.device, dtype=torch.float64)
+    sinusoid = torch.outer(position, torch.pow(10000, -idx.div(half)))
     return torch.cat([torch.cos(sinusoid), torch.sin(sinusoid)], dim=1)
 
 
@@ -180,8 +182,7 @@ class OSPNextCrossAttention(OSPNextSelfAttention):
             from ..quant.hif8 import hif8_qkv
             q, k, v = hif8_qkv(q, k, v, getattr(self, "scale_max_forward", 15.0),
                                getattr(self, "scale_max_backward", 224.0))
-        seg_q = torch.tensor([0, n], dtype=torch.int32)
-        seg_k = torch.tensor([0, k.shape[1]], dtype=torch.int32)
+        seg_q, seg_k = _one_segment(n), _one_segment(k.shape[1])
         if x.is_cuda:
             q, k, v = q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16)
         return Fn.attention(q, k, v, seg_q, seg_k).flatten(2)
@@ -451,7 +452,7 @@ class OSPNextModel(nn.Module):
         prev_kind = None
         # rows of the first layout (every rank computed the full patch embedding)
         first = make_layout(self.block_kinds[0], grid, P, spec)
-        x = x[:, first.tokens.to(device)] if not _is_arange(first.tokens, x.shape[1]) else x
+        x = x[:, _dev(first.tokens, device, torch.long)] if not _is_arange(first.tokens, x.shape[1]) else x
         prev_kind = self.block_kinds[0]
         nb = len(self.blocks)
         for i, block in enumerate(self.blocks):
@@ -494,7 +495,7 @@ class OSPNextModel(nn.Module):
 
     def _context(self, kind, grid, spec, device, freqs) -> BlockContext:
         lay = make_layout(kind, grid, self.sparse_ratio, spec)
-        pos = _dev(token_positions(lay.tokens, grid), device, torch.int32)
+        pos = _dev(_layout_positions(kind, tuple(grid), self.sparse_ratio, spec), device, torch.int32)
         seg = lay.seg
         ug = None
         if lay.a2a_splits is not None and self.parallel is not None:
@@ -528,10 +529,24 @@ def _is_arange(idx: torch.Tensor, n: int) -> bool:
 _DEV_CACHE = {}
 
 
+@functools.lru_cache(maxsize=256)
+def _layout_positions(kind, grid, P, spec) -> torch.Tensor:
+    """(t, h, w) of a layout's tokens; one CPU tensor per layout, so its device copy is cached."""
+    return token_positions(make_layout(kind, grid, P, spec).tokens, grid)
+
+
+@functools.lru_cache(maxsize=64)
+def _one_segment(n: int) -> torch.Tensor:
+    """Segment table [0, n] (one CPU tensor per length, so its device copy is cached)."""
+    return torch.tensor([0, n], dtype=torch.int32)
+
+
 def _dev(t: torch.Tensor, device, dtype):
     key = (id(t), str(device), dtype)
     v = _DEV_CACHE.get(key)
     if v is None or v[0] is not t:
+        if len(_DEV_CACHE) > 4096:       # inputs are cached host tables; bound it all the same
+            _DEV_CACHE.clear()
         v = (t, t.to(device=device, dtype=dtype))
         _DEV_CACHE[key] = v
     return v[1]

@@ -8,19 +8,21 @@
 // ever made and padded tokens never exist (they are not in any segment).
 //
 // CTA = 2 query tiles of 128 rows (one head, one segment, one batch entry).
-//   warp 0       TMA producer: Q0,Q1 once; then K_j, V_j into a 3-slot ring
+//   warp 0       TMA producer: Q0,Q1 once; then K_j, V_j into a 5-slot ring
 //   warp 1       MMA issuer:   S_t = Q_t·K_jᵀ (TMEM, fp32), O_t += P_t·V_j (TMEM, fp32)
 //   warps 4..7   softmax group 0 (tile 0), warps 8..11 softmax group 1 (tile 1):
 //                thread ↔ query row (warp w reads TMEM lanes 32·(w mod 4)…);
 //                S row from TMEM, online softmax in the exp2 domain with lazy O
 //                rescaling (only when the running max grows by more than 2^8),
-//                P written bf16 to 128B-swizzled smem; epilogue O/l → bf16, LSE.
+//                P written bf16 back into TMEM over S (tcgen05.st); epilogue O/l → bf16, LSE.
+// The PV MMA takes P from TMEM (A operand) and V from smem, so P never touches
+// shared memory; the 64 KiB this frees deepens the K/V ring to five slots.
 // The tensor core alternates tile 0 / tile 1 work so each softmax group overlaps
 // the other tile's MMAs.  TMEM: S0 | S1 | O0 | O1 (512 columns for D = 128).
 // Softmax: one S row (128 fp32) per thread from four TMEM loads and one wait;
 // full KV tiles skip the per-column key mask; 3-input max, packed f32x2 FMA/ADD
 // (sm_100a) for the scale/shift, the row sum and the FMA-pipe exponentials.
-// A quarter of the exponentials run on the FMA pipe (exp2_poly) instead of MUFU.
+// A share of the exponentials (OSP_ATTN_POLY_MASK) runs on the FMA/ALU pipes (exp2_fma2).
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -32,7 +34,7 @@ namespace osp {
 
 constexpr int kQT = 128;      // rows per query tile
 constexpr int kKT = 128;      // keys per KV tile
-constexpr int kSlots = 3;     // K/V ring slots
+constexpr int kSlots = 5;     // K/V ring slots (the smem freed by keeping P in TMEM)
 constexpr int kAttnThreads = 384;
 
 struct AttnArgs {
@@ -49,21 +51,6 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// 2^x on the FMA pipe: Cody–Waite split x = n + f (n = ⌊x⌋, f ∈ [0,1)), a cubic
-// fitted to 2^f on [0,1] by iteratively reweighted least squares on Chebyshev
-// nodes (max relative error 7.5e-5, far below bf16's 3.9e-3), and 2^n added to the
-// exponent field.  Inputs below −126 flush to 0 (P entries that small vanish in bf16).
-__device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -126.0f);
-  const float n = floorf(x);
-  const float f = x - n;
-  float p = fmaf(f, 0.07802443951368332f, 0.22606734931468964f);
-  p = fmaf(p, f, 0.6958334445953369f);
-  p = fmaf(p, f, 0.9999252557754517f);
-  const int e = __float2int_rn(n) << 23;
-  return __int_as_float(__float_as_int(p) + e);
 }
 
 // Packed fp32x2 helpers (sm_100a FFMA2 / FADD2): two lanes of math per instruction.
@@ -90,21 +77,113 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
-// exp2 of a pair on the FMA pipe (same method as exp2_poly, polynomial in f32x2)
-__device__ __forceinline__ uint64_t exp2_poly2(float x0, float x1) {
-  x0 = fmaxf(x0, -126.0f);
-  x1 = fmaxf(x1, -126.0f);
-  const float n0 = floorf(x0), n1 = floorf(x1);
-  const uint64_t f = fadd2(pk2(x0, x1), pk2(-n0, -n1));
-  uint64_t p = ffma2(f, pk2(0.07802443951368332f, 0.07802443951368332f),
-                     pk2(0.22606734931468964f, 0.22606734931468964f));
-  p = ffma2(p, f, pk2(0.6958334445953369f, 0.6958334445953369f));
-  p = ffma2(p, f, pk2(0.9999252557754517f, 0.9999252557754517f));
-  float p0, p1;
+// 2^x for a pair on the FMA/ALU pipes, no MUFU and no float↔int conversion:
+// adding 1.5·2²³ rounds x to the nearest integer n inside the mantissa of j, f = x − n
+// lies in [−½, ½], a cubic gives 2^f, and (bits(j) << 23) = n << 23 (the magic
+// constant's bits shift out) is added to the exponent field.  The cubic is our own
+// relative-error minimax fit of 2^f on [−½, ½] (iteratively reweighted least squares),
+// max relative error 7.5e-5 (1.4e-4 through this fp32 path), far below bf16's 3.9e-3.
+// x is clamped at −125 so the exponent never underflows (such P entries are 0 in bf16).
+__device__ __forceinline__ uint64_t exp2_fma2(float x0, float x1) {
+  const uint64_t x = pk2(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+  const uint64_t j = fadd2(x, pk2(12582912.0f, 12582912.0f));
+  const uint64_t n = fadd2(j, pk2(-12582912.0f, -12582912.0f));
+  const uint64_t f = ffma2(n, pk2(-1.0f, -1.0f), x);
+  uint64_t p = ffma2(f, pk2(0.055170949548482895f, 0.055170949548482895f),
+                     pk2(0.2426096349954605f, 0.2426096349954605f));
+  p = ffma2(p, f, pk2(0.6932609677314758f, 0.6932609677314758f));
+  p = ffma2(p, f, pk2(0.9999281764030457f, 0.9999281764030457f));
+  float p0, p1, j0, j1;
   upk2(p, p0, p1);
-  p0 = __int_as_float(__float_as_int(p0) + (__float2int_rn(n0) << 23));
-  p1 = __int_as_float(__float_as_int(p1) + (__float2int_rn(n1) << 23));
-  return pk2(p0, p1);
+  upk2(j, j0, j1);
+  return pk2(__int_as_float(__float_as_int(p0) + (__float_as_int(j0) << 23)),
+             __int_as_float(__float_as_int(p1) + (__float_as_int(j1) << 23)));
+}
+
+// Which 8-column groups (bit c16 mod 8) take exp2_fma2 instead of MUFU ex2.  Measured at
+// the 14B shapes (TFLOP/s, same box): 1 group in 8 → 1062, none → 1056, 2 → 1019,
+// 3 → 998; 4 and 5 slower still.  The softmax is issue-bound, and a polynomial
+// exponential costs ~5 issue slots where MUFU costs one.
+#ifndef OSP_ATTN_POLY_MASK
+#define OSP_ATTN_POLY_MASK 0x80
+#endif
+
+__device__ __forceinline__ float exp2_fma(float x) {     // scalar form of exp2_fma2
+  x = fmaxf(x, -125.0f);
+  const float j = x + 12582912.0f;
+  const float f = x - (j - 12582912.0f);
+  float p = fmaf(f, 0.055170949548482895f, 0.2426096349954605f);
+  p = fmaf(p, f, 0.6932609677314758f);
+  p = fmaf(p, f, 0.9999281764030457f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(j) << 23));
+}
+
+// Packed f32x2 (1) or scalar (0) scale/shift and row sum: equal speed when measured.
+#ifndef OSP_ATTN_PACKED
+#define OSP_ATTN_PACKED 1
+#endif
+
+// One S row (128 fp32 in registers) → P = 2^(s·scale·log2e − m) as bf16 pairs stored over
+// the S columns in TMEM (taddr = this warp's lanes of S_t); returns the row sum of P.
+// kFull: all 128 keys valid (no per-column mask in the hot path).
+template <bool kFull>
+__device__ __forceinline__ float softmax_p_to_tmem(const uint32_t* sr, float sl2, float m, int n_valid,
+                                                   uint32_t taddr) {
+#if OSP_ATTN_PACKED
+  const uint64_t sl2x2 = pk2(sl2, sl2), negm2 = pk2(-m, -m);
+  uint64_t ls2 = pk2(0.f, 0.f);
+#pragma unroll
+  for (int c16 = 0; c16 < kKT / 8; ++c16) {
+    uint32_t pw[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int c = c16 * 8 + 2 * i;
+      const uint64_t xe = ffma2(pk2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sl2x2, negm2);
+      float x0, x1;
+      upk2(xe, x0, x1);
+      uint64_t e;
+      if ((OSP_ATTN_POLY_MASK >> (c16 & 7)) & 1) e = exp2_fma2(x0, x1);
+      else e = pk2(ex2(x0), ex2(x1));
+      float e0, e1;
+      upk2(e, e0, e1);
+      if (!kFull) {
+        e0 = c < n_valid ? e0 : 0.f;
+        e1 = c + 1 < n_valid ? e1 : 0.f;
+        e = pk2(e0, e1);
+      }
+      ls2 = fadd2(ls2, e);
+      pw[i] = pack_bf16x2(e0, e1);
+    }
+    tmem_st4(taddr + c16 * 4, pw[0], pw[1], pw[2], pw[3]);   // 8 keys → 4 TMEM columns
+  }
+  float a, b;
+  upk2(ls2, a, b);
+  return a + b;
+#else
+  float ls[4] = {0.f, 0.f, 0.f, 0.f};
+  const float negm = -m;
+#pragma unroll
+  for (int c16 = 0; c16 < kKT / 8; ++c16) {
+    uint32_t pw[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int c = c16 * 8 + 2 * i;
+      const float x0 = fmaf(__uint_as_float(sr[c]), sl2, negm);
+      const float x1 = fmaf(__uint_as_float(sr[c + 1]), sl2, negm);
+      const bool poly = (OSP_ATTN_POLY_MASK >> (c16 & 7)) & 1;
+      float e0 = poly ? exp2_fma(x0) : ex2(x0);
+      float e1 = poly ? exp2_fma(x1) : ex2(x1);
+      if (!kFull) {
+        e0 = c < n_valid ? e0 : 0.f;
+        e1 = c + 1 < n_valid ? e1 : 0.f;
+      }
+      ls[i] += e0 + e1;
+      pw[i] = pack_bf16x2(e0, e1);
+    }
+    tmem_st4(taddr + c16 * 4, pw[0], pw[1], pw[2], pw[3]);
+  }
+  return (ls[0] + ls[1]) + (ls[2] + ls[3]);
+#endif
 }
 
 template <int D>
@@ -113,11 +192,9 @@ struct AttnSmem {
   static constexpr int DB = D / 64;                     // boxes per row of D
   static constexpr int Q_TILE = DB * BOX;
   static constexpr int KV_SLOT = DB * BOX;
-  static constexpr int P_TILE = 2 * BOX;                // 128 keys = 2 boxes
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_KV = OFF_Q + 2 * Q_TILE;
-  static constexpr int OFF_P = OFF_KV + kSlots * KV_SLOT;
-  static constexpr int OFF_BAR = OFF_P + 2 * P_TILE;
+  static constexpr int OFF_BAR = OFF_KV + kSlots * KV_SLOT;
   static constexpr int BYTES = OFF_BAR + 256 + 1024;   // barriers + alignment slack
 };
 
@@ -144,17 +221,16 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
   uint8_t* smem = smem_raw + ((1024u - (base_u32 & 1023u)) & 1023u);
   uint8_t* sQ = smem + L::OFF_Q;
   uint8_t* sKV = smem + L::OFF_KV;
-  uint8_t* sP = smem + L::OFF_P;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;            // [3]
-  uint64_t* kv_empty = bars + 4;           // [3]
-  uint64_t* s_full = bars + 7;             // [2]
-  uint64_t* p_full = bars + 9;             // [2]
-  uint64_t* pv_done = bars + 11;           // [2]
-  uint64_t* done = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 15);
+  uint64_t* kv_full = bars + 1;                    // [kSlots]
+  uint64_t* kv_empty = kv_full + kSlots;           // [kSlots]
+  uint64_t* s_full = kv_empty + kSlots;            // [2]
+  uint64_t* p_full = s_full + 2;                   // [2]
+  uint64_t* pv_done = p_full + 2;                  // [2]
+  uint64_t* done = pv_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(done + 2);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -212,16 +288,15 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           umma_bf16(d, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(ka + off, 16, 1024), ID_S, k > 0 ? 1u : 0u);
         }
       };
+      // O_t += P_t·V: P_t (bf16, written by the softmax group over the first 64 columns of
+      // S_t) is the A operand straight from TMEM, 8 columns = 16 keys per step
       auto issue_pv = [&](int t, int slot, bool acc) {
-        const uint32_t pa = smem_u32(sP + t * L::P_TILE);
         const uint32_t va = smem_u32(sKV + slot * L::KV_SLOT);
         const uint32_t d = tmem + 256u + (uint32_t)D * t;
+        const uint32_t pa = tmem + 128u * t;
 #pragma unroll
-        for (int k = 0; k < kKT / 16; ++k) {
-          const uint32_t poff = (k / 4) * L::BOX + (k % 4) * 32;
-          umma_bf16(d, sdesc_sw128(pa + poff, 16, 1024), sdesc_sw128(va + k * 2048, L::BOX, 1024), ID_PV,
-                    (acc || k > 0) ? 1u : 0u);
-        }
+        for (int k = 0; k < kKT / 16; ++k)
+          umma_bf16_ts(d, pa + 8u * k, sdesc_sw128(va + k * 2048, L::BOX, 1024), ID_PV, (acc || k > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(q_full, 0, args.err, kErrAttnMma);
       // prologue: S0(0), S1(0)
@@ -276,7 +351,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     const uint32_t tOt = tmem + 256u + (uint32_t)D * t;
     const float sl2 = args.scale_log2;
     float m_ref = -INFINITY, l = 0.f;
-    uint8_t* pT = sP + t * L::P_TILE;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       if (!(ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, args.err, kErrAttnSoftmax)))) break;
@@ -290,13 +364,14 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       tmem_ld_wait();
       float mx;
       if (full_tile) {
-        float m2[2] = {-INFINITY, -INFINITY};
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};   // 4 independent chains
 #pragma unroll
-        for (int c = 0; c < kKT; c += 4) {
-          m2[0] = max3(m2[0], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
-          m2[1] = max3(m2[1], __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+        for (int c = 0; c < kKT; c += 8) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            m4[q] = max3(m4[q], __uint_as_float(sr[c + 2 * q]), __uint_as_float(sr[c + 2 * q + 1]));
         }
-        mx = fmaxf(m2[0], m2[1]);
+        mx = max3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
       } else {
         mx = -INFINITY;
 #pragma unroll
@@ -325,46 +400,11 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         }
       }
       m_ref = m_new;
-      // P = exp2(s·scale·log2e − m_ref) → bf16, 128B-swizzled K-major rows.  Scale/shift and
-      // the row sum run as packed f32x2; every fourth 8-column group uses the FMA-pipe exp2.
-      const uint64_t sl2x2 = pk2(sl2, sl2), negm2 = pk2(-m_ref, -m_ref);
-      uint64_t ls2 = pk2(0.f, 0.f);
-#pragma unroll
-      for (int c16 = 0; c16 < kKT / 8; ++c16) {
-        uint64_t pp[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int c = c16 * 8 + 2 * i;
-          const uint64_t xe = ffma2(pk2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sl2x2, negm2);
-          float x0, x1;
-          upk2(xe, x0, x1);
-          uint64_t e;
-          if ((c16 & 3) == 3) e = exp2_poly2(x0, x1);
-          else e = pk2(ex2(x0), ex2(x1));
-          if (!full_tile) {
-            float e0, e1;
-            upk2(e, e0, e1);
-            e = pk2(c < n_valid ? e0 : 0.f, c + 1 < n_valid ? e1 : 0.f);
-          }
-          pp[i] = e;
-          ls2 = fadd2(ls2, e);
-        }
-        float p[8];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) upk2(pp[i], p[2 * i], p[2 * i + 1]);
-        uint4 w;
-        w.x = pack_bf16x2(p[0], p[1]);
-        w.y = pack_bf16x2(p[2], p[3]);
-        w.z = pack_bf16x2(p[4], p[5]);
-        w.w = pack_bf16x2(p[6], p[7]);
-        const int box = c16 >> 3, chunk = c16 & 7;
-        *reinterpret_cast<uint4*>(pT + box * L::BOX + r * 128 + ((chunk ^ (r & 7)) << 4)) = w;
-      }
-      float ls_a, ls_b;
-      upk2(ls2, ls_a, ls_b);
-      const float lsum = ls_a + ls_b;
+      // P = exp2(s·scale·log2e − m_ref) → bf16 pairs stored into TMEM over S
+      const float lsum = full_tile ? softmax_p_to_tmem<true>(sr, sl2, m_ref, n_valid, tSt + lane_off)
+                                   : softmax_p_to_tmem<false>(sr, sl2, m_ref, n_valid, tSt + lane_off);
       l += lsum;
-      fence_proxy_async_smem();
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);

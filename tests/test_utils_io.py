@@ -58,8 +58,8 @@ def test_cuda_graph_sampling_matches_eager():
     from osp_next_b200.schedulers.flow_matching import FlowMatchingScheduler
     torch.manual_seed(0)
     with torch.device("cuda"):
-        m = OSPNextModel(dim=256, ffn_dim=512, num_heads=2, num_layers=4, text_len=16,
-                         skiparse_model_type="dual_end", sparse_ratio=2, num_full_blocks=2)
+        m = OSPNextModel(dim=256, ffn_dim=512, num_heads=2, num_layers=8, text_len=16,
+                         skiparse_model_type="dual_end", sparse_ratio=2, num_full_blocks=4)
     m = m.to(torch.bfloat16).eval()
     x = torch.randn(1, 16, 3, 16, 16, device="cuda")
     c = torch.randn(1, 16, 4096, device="cuda", dtype=torch.bfloat16)
