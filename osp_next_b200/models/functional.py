@@ -143,43 +143,25 @@ def apply_rope(x, pos, freqs):
 # ----------------------------------------------------------------------------- attention
 
 class _AttnFn(torch.autograd.Function):
-    """Segmented attention: forward on the tcgen05 flash kernel, backward by
-    recomputation of each segment with exact softmax gradients in fp32 blocks."""
+    """Segmented attention with both passes on the tcgen05 kernels: the forward keeps
+    (q, k, v, o, LSE) in bf16/fp32, the backward recomputes P from the LSE."""
 
     @staticmethod
     def forward(ctx, q, k, v, seg_q, seg_k, scale):
-        o, lse = ops.attention(q.to(_BF16), k.to(_BF16), v.to(_BF16), seg_q, seg_k, scale, return_lse=True)
-        ctx.save_for_backward(q, k, v, o, lse)
-        ctx.seg_q = seg_q.tolist()
-        ctx.seg_k = seg_k.tolist()
+        qb, kb, vb = q.to(_BF16), k.to(_BF16), v.to(_BF16)
+        o, lse = ops.attention(qb, kb, vb, seg_q, seg_k, scale, return_lse=True)
+        ctx.save_for_backward(qb, kb, vb, o, lse)
+        ctx.segs = (seg_q, seg_k)
         ctx.scale = scale
+        ctx.dtypes = (q.dtype, k.dtype, v.dtype)
         return o
 
     @staticmethod
     def backward(ctx, go):
         q, k, v, o, lse = ctx.saved_tensors
-        dq = torch.zeros_like(q, dtype=torch.float32)
-        dk = torch.zeros_like(k, dtype=torch.float32)
-        dv = torch.zeros_like(v, dtype=torch.float32)
-        sq, sk = ctx.seg_q, ctx.seg_k
-        scale = ctx.scale
-        # delta_i = rowsum(dO ∘ O)
-        delta = (go.float() * o.float()).sum(-1).transpose(1, 2)          # B,H,nq
-        QB = 2048
-        for s in range(len(sq) - 1):
-            ks = k[:, sk[s]:sk[s + 1]].float().transpose(1, 2)            # B,H,Lk,D
-            vs = v[:, sk[s]:sk[s + 1]].float().transpose(1, 2)
-            for q0 in range(sq[s], sq[s + 1], QB):
-                q1 = min(q0 + QB, sq[s + 1])
-                qs = q[:, q0:q1].float().transpose(1, 2)
-                g = go[:, q0:q1].float().transpose(1, 2)
-                p = torch.exp(qs @ ks.transpose(-1, -2) * scale - lse[:, :, q0:q1, None])
-                dv[:, sk[s]:sk[s + 1]] += (p.transpose(-1, -2) @ g).transpose(1, 2)
-                dp = g @ vs.transpose(-1, -2)
-                ds = p * (dp - delta[:, :, q0:q1, None]) * scale
-                dq[:, q0:q1] = (ds @ ks).transpose(1, 2)
-                dk[:, sk[s]:sk[s + 1]] += (ds.transpose(-1, -2) @ qs).transpose(1, 2)
-        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, None, None
+        dq, dk, dv = ops.attention_bwd(q, k, v, o, go, lse, ctx.segs[0], ctx.segs[1], ctx.scale)
+        tq, tk, tv = ctx.dtypes
+        return dq.to(tq), dk.to(tk), dv.to(tv), None, None, None
 
 
 def attention(q, k, v, seg_q, seg_k, scale=None):

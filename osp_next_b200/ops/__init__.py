@@ -189,6 +189,27 @@ def attention(q, k, v, seg_q, seg_k, scale: Optional[float] = None, return_lse: 
     return (out, lse) if return_lse else out
 
 
+def attention_bwd(q, k, v, o, dout, lse, seg_q, seg_k, scale: Optional[float] = None):
+    """Gradients (dq, dk, dv) of :func:`attention` on the tcgen05 backward kernels.
+
+    q [B,nq,H,D], k/v [B,nk,H,D] bf16 (row-strided views allowed), o/dout contiguous
+    [B,nq,H,D] bf16, lse [B,H,nq] fp32 from the forward.  Returns contiguous bf16 grads.
+    """
+    D = q.shape[-1]
+    scale = scale if scale is not None else 1.0 / math.sqrt(D)
+    if not _cuda(q):
+        return ref.attention_bwd(q, k, v, dout, seg_q, seg_k, scale)
+    dq = torch.empty(q.shape, dtype=_BF16, device=q.device)
+    dk = torch.empty(k.shape, dtype=_BF16, device=q.device)
+    dv = torch.empty(v.shape, dtype=_BF16, device=q.device)
+    delta = torch.empty(q.shape[0], q.shape[2], q.shape[1], dtype=torch.float32, device=q.device)
+    sq, max_q = _seg_dev(seg_q, q.device)
+    sk, max_k = _seg_dev(seg_k, q.device)
+    ext().attention_bwd(q, k, v, _c(o.to(_BF16)), _c(dout.to(_BF16)), _c(lse.float()), sq, sk, dq, dk, dv, delta,
+                        float(scale), max_q, max_k)
+    return dq, dk, dv
+
+
 def sde_step(x, v, sigma: float, dt: float, sigma_min: float, sigma_max: float, noise=None, prev_sample=None):
     """Fused GRPO SDE step (CUDA) → (prev_sample f32, log_prob [B] f32, mean f32)."""
     x = _c(x.float())

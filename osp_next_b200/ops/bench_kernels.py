@@ -17,7 +17,7 @@ import statistics
 
 import torch
 
-from . import attention, linear, linear_gated_residual, ln_modulate, qk_norm_rope
+from . import attention, attention_bwd, linear, linear_gated_residual, ln_modulate, qk_norm_rope
 from .reference import rope_freqs
 
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
@@ -95,6 +95,19 @@ def cases(size: str):
             return (lambda: attention(q, k, v, sq, sk)), fl, (q.numel() * 4 + k.numel() * 4) * 2
         return setup
 
+    def attn_bwd(lengths):
+        # algorithmic FLOPs of the backward: 5 matmuls of 2·L²·D per head (S, dP, dV, dK, dQ)
+        def setup():
+            n = sum(lengths)
+            q = torch.randn(B, n, H, D, device=dev, dtype=bf)
+            k, v = torch.randn_like(q), torch.randn_like(q)
+            sq = _segs(lengths, dev)
+            o, lse = attention(q, k, v, sq, sq, return_lse=True)
+            g = torch.randn_like(q)
+            fl = 10.0 * B * H * sum(L * L for L in lengths) * D
+            return (lambda: attention_bwd(q, k, v, o, g, lse, sq, sq)), fl, q.numel() * 2 * 8
+        return setup
+
     def lnmod():
         x = torch.randn(B, N, C, device=dev)
         sh, sc = torch.randn(B, C, device=dev), torch.randn(B, C, device=dev)
@@ -117,6 +130,8 @@ def cases(size: str):
         "attn_sparse": attn([G, G, G, G]),
         "attn_dense": attn([N]),
         "attn_cross": attn([N], nk=512),
+        "attn_sparse_bwd": attn_bwd([G, G, G, G]),
+        "attn_dense_bwd": attn_bwd([N]),
         "ln_modulate": lnmod,
         "qk_norm_rope": qkrope,
     }

@@ -17,6 +17,10 @@ void qk_norm_rope(at::Tensor& qkv, const at::Tensor& wq, const at::Tensor& wk, c
                   const at::Tensor& freqs, int64_t num_heads, double eps);
 void attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& seg_q,
                    const at::Tensor& seg_k, at::Tensor& out, at::Tensor& lse, double scale, int64_t max_q);
+void attention_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+                   const at::Tensor& dout, const at::Tensor& lse, const at::Tensor& seg_q, const at::Tensor& seg_k,
+                   at::Tensor& dq, at::Tensor& dk, at::Tensor& dv, at::Tensor& delta, double scale, int64_t max_q,
+                   int64_t max_k);
 void cfg_euler(const at::Tensor& lat, const at::Tensor& cond, const at::Tensor& unc, at::Tensor& out, double g,
                double dt);
 void hif8_round(const at::Tensor& x, at::Tensor& out, double s);
@@ -69,6 +73,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rms_norm", &osp::rms_norm);
   m.def("qk_norm_rope", &osp::qk_norm_rope);
   m.def("attention_fwd", &osp::attention_fwd);
+  m.def("attention_bwd", &osp::attention_bwd);
   m.def("cfg_euler", &osp::cfg_euler);
   m.def("hif8_round", &osp::hif8_round);
   m.def("hif8_qdq", &osp::hif8_qdq);

@@ -160,6 +160,24 @@ def attention(q, k, v, seg_q: torch.Tensor, seg_k: torch.Tensor, scale: Optional
     return (o, lse) if return_lse else o
 
 
+def attention_bwd(q, k, v, dout, seg_q: torch.Tensor, seg_k: torch.Tensor, scale: Optional[float] = None):
+    """fp32 gradients (dq, dk, dv) of :func:`attention` by autograd of the same math."""
+    D = q.shape[-1]
+    scale = scale if scale is not None else 1.0 / math.sqrt(D)
+    qf, kf, vf = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    sq, sk = seg_q.tolist(), seg_k.tolist()
+    outs = []
+    for s in range(len(sq) - 1):
+        qs = qf[:, sq[s]:sq[s + 1]].transpose(1, 2)
+        ks = kf[:, sk[s]:sk[s + 1]].transpose(1, 2)
+        vs = vf[:, sk[s]:sk[s + 1]].transpose(1, 2)
+        p = torch.softmax((qs @ ks.transpose(-1, -2)) * scale, dim=-1)
+        outs.append((p @ vs).transpose(1, 2))
+    o = torch.cat(outs, dim=1)
+    o.backward(dout.float())
+    return qf.grad, kf.grad, vf.grad
+
+
 def cfg_euler_step(latents, cond, uncond, guidance: float, dt: float):
     """``x + (u + g·(c−u))·dt`` in fp32, cast back (flow_matching.py:116-127, 178-184)."""
     v = uncond.float() + guidance * (cond.float() - uncond.float())
