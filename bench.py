@@ -63,6 +63,8 @@ def parse():
     p.add_argument("--guidance", type=float, default=5.0)
     p.add_argument("--shift", type=float, default=5.0)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--mode", choices=["infer", "train"], default="infer",
+                   help="infer: the sec/video headline; train: flow-matching training tokens/s")
     p.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                    help="SSP layout exchange: fused GEMM-epilogue stores over NVLink, or NCCL all_to_all")
     return p.parse_args()
@@ -125,7 +127,7 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- helpers
 
-def init_dist(n):
+def init_dist(n, backend="nccl"):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world != n:
         raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}; launch with torchrun --nproc-per-node {n}")
@@ -134,7 +136,7 @@ def init_dist(n):
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
     return rank, world, local
 
@@ -253,6 +255,91 @@ def run_ours(args, rank, world, local):
     return ms, launches, clocks, e2e, {"finite": finite, "device_error": err}
 
 
+# ----------------------------------------------------------------------------- training
+
+TRAIN_CONFIGS = {"14b": "configs/train/osp_14b.yaml", "1.3b": "configs/train/osp_1_3b.yaml",
+                 "tiny": "configs/train/osp_tiny_cpu.yaml"}
+
+
+def train_layout(world: int):
+    """(fsdp, ssp) per GPU count for training: FSDP over every rank, SSP up to 4
+    (8 GPUs = 2 SSP groups of 4 as data parallel, the reference's 14B layout)."""
+    return world, min(world, 4)
+
+
+def train_config(args, world, out_dir):
+    from osp_next_b200.utils.config import load_config
+    cfg = load_config(os.path.join(ROOT, TRAIN_CONFIGS[args.model]))
+    fsdp, ssp = train_layout(world)
+    cfg.update(output_dir=out_dir, training_iteration=10 ** 9, max_steps=args.warmup + args.steps,
+               save_interval=10 ** 9, log_interval=1, fsdp_size=fsdp, skiparse_sp_size=ssp,
+               use_skiparse_sequence_parallel=ssp > 1, sp_size=1, use_sequence_parallel=False,
+               weight_dtype="bf16", gradient_checkpointing=True, seed=1024)
+    cfg["model_config"] = dict(cfg.get("model_config", {}), **{k: v for k, v in PRESETS[args.model].items()})
+    cfg["model_config"].pop("pretrained_model_dir_or_checkpoint", None)
+    dc = dict(cfg.get("data_config", {}))
+    dc.update(dataset_name="t2v_random_latent", num_workers=2, pin_memory=True, batch_size=1,
+              dataset_config=dict(sample_height=args.height, sample_width=args.width,
+                                  sample_num_frames=args.frames, text_max_length=PRESETS[args.model]["text_len"]))
+    cfg["data_config"] = dc
+    return cfg
+
+
+def run_train(args, rank, world, local, impl):
+    """Flow-matching training through the public trainer (``train/train_osp.py``): every
+    step loads a synthetic latent/text batch from pinned host memory, runs the FSDP2 + SSP
+    forward/backward with activation checkpointing, clips, AdamW, EMA, and reads the loss
+    back.  tokens/s = tokens of all data-parallel groups / device step time (max over ranks)."""
+    import tempfile
+    sys.path.insert(0, os.path.join(ROOT, "train"))
+    out_dir = tempfile.mkdtemp(prefix="osp_bench_train_")
+    cfg = train_config(args, world, out_dir)
+    rec = []
+    clock = ClockSampler(local)
+
+    def on_step(it, ms, tok):
+        if it == args.warmup:
+            clock.start()
+        if it > args.warmup:
+            rec.append((ms, tok, time.perf_counter()))
+
+    t_first = [None]
+
+    def on_step_wall(it, ms, tok):
+        if it == args.warmup:
+            t_first[0] = time.perf_counter()
+        on_step(it, ms, tok)
+
+    if impl == "reference":
+        sys.path.insert(0, os.path.join(ROOT, "baseline"))
+        import ref_harness
+        if not os.path.isdir(os.path.join(ref_harness.REF_ROOT, "ospnext")):
+            return {"metric": "train tokens/s", "impl": "reference", "unavailable": "reference not installed"}
+        import ref_train
+        ref_train.train(cfg, on_step_wall)
+    else:
+        import train_osp
+        train_osp.main(cfg, on_step=on_step_wall)
+    clocks = clock.stop()
+    ms = max_over_ranks(sum(r[0] for r in rec) / len(rec))
+    tok = rec[-1][1]
+    wall = max_over_ranks((rec[-1][2] - t_first[0]) / len(rec))
+    fsdp, ssp = train_layout(world)
+    return {"metric": f"train tokens/s OSP-Next-{args.model} flow matching {args.frames}f "
+                      f"{args.height}x{args.width}", "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak" if world > 4 else "strong",
+            "dtype": "bf16", "impl": impl,
+            "data": "synthetic (random-init weights, N(0,1) latents and text embeddings, logit-normal t)",
+            "config": {"model": f"OSP-Next-{args.model}", "global_batch": max(1, world // ssp),
+                       "seq_len": tokens(args), "parallelism": f"fsdp{fsdp}_ssp{ssp}_dp{max(1, world // ssp)}",
+                       "activation_checkpointing": True, "optimizer": "AdamW + adaptive clip + EMA",
+                       "l2": "no flush: per-step activations exceed the 126 MB L2"},
+            "value": round(tok / (ms / 1000.0), 1), "ms_per_step": round(ms, 2), "vs_baseline": None,
+            "clocks": clocks,
+            "e2e": {"value": round(tok / wall, 1), "unit": "tokens/s",
+                    "note": "host wall time per trainer step (pinned-host batch copy, loss read back)"}}
+
+
 # ----------------------------------------------------------------------------- reference
 
 def run_reference(args, rank, world, local):
@@ -260,7 +347,8 @@ def run_reference(args, rank, world, local):
     import ref_harness
     if not os.path.isdir(os.path.join(ref_harness.REF_ROOT, "ospnext")):
         return None, "reference not installed in baseline/_ref"
-    osp, fm = ref_harness.import_reference(disable_compile=False, force_sdpa=not ref_harness.fa2_usable())
+    fa2 = ref_harness.fa2_usable()
+    osp, fm = ref_harness.import_reference(disable_compile=False, force_sdpa=not fa2)
     cfg = dict(PRESETS[args.model])
     dev = torch.device("cuda", local)
     if world > 1:
@@ -300,6 +388,7 @@ def run_reference(args, rank, world, local):
         barrier_sync()
         clocks = clock.stop()
     ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+    clocks["attention_backend"] = "flash_attn2" if fa2 else "sdpa"
     return (ms, clocks), None
 
 
@@ -307,7 +396,21 @@ def run_reference(args, rank, world, local):
 
 def main():
     args = parse()
-    rank, world, local = init_dist(args.gpus)
+    # training also gathers CPU objects (loss logs, sampler state): gloo beside NCCL
+    rank, world, local = init_dist(args.gpus, "cpu:gloo,cuda:nccl" if args.mode == "train" else "nccl")
+    if args.mode == "train":
+        if args.model == "14b" and world == 1:
+            line = {"metric": "train tokens/s OSP-Next-14b", "n_gpus": 1, "impl": args.impl,
+                    "unavailable": "14B AdamW training state (fp32 params, grads, moments, EMA: ~285 GB) "
+                                   "does not fit one 180 GB GPU; needs FSDP over >= 2 GPUs"}
+        else:
+            line = run_train(args, rank, world, local, args.impl)
+        if rank == 0:
+            print(json.dumps(line))
+        if dist.is_initialized():
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     cfg_size, ssp = layout_for(world)
     par = {1: "single", 2: "cfg2", 4: "cfg2_ssp2", 8: "cfg2_ssp4"}[world]
     if world >= 4 and args.impl == "ours":

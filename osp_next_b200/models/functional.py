@@ -9,7 +9,8 @@ Three paths, chosen per call:
   :mod:`osp_next_b200.ops` (bf16 operands, fp32 accumulation, fp32 residual).
 * CUDA with autograd (training): :class:`torch.autograd.Function` wrappers whose
   forward runs the same kernels; GEMM backward runs on the same tcgen05 GEMM
-  (on transposed operands); norm/RoPE backward is written in PyTorch.
+  (reading dY, W and X MN-major in place); attention backward on its own tcgen05
+  kernels; norm/RoPE backward is written in PyTorch.
 """
 from __future__ import annotations
 
@@ -49,7 +50,11 @@ class _LinearFn(torch.autograd.Function):
     def forward(ctx, x, w, b, act):
         x2 = x.reshape(-1, x.shape[-1]).to(_BF16)
         wb = w.to(_BF16)
-        if act == "gelu_tanh":
+        if act == "gelu_tanh" and w.shape[0] % 32 == 0 and x2.shape[1] % 8 == 0:
+            # one GEMM writes gelu(pre) and pre (bf16, as the reference's autocast Linear output)
+            y, pre = ops.linear_gelu_aux(x2, wb, b)
+            ctx.save_for_backward(x2, wb, pre)
+        elif act == "gelu_tanh":
             pre = ops.linear(x2, wb, b, None, out_dtype=torch.float32)
             y = F.gelu(pre, approximate="tanh").to(_BF16)
             ctx.save_for_backward(x2, wb, pre)
@@ -67,17 +72,99 @@ class _LinearFn(torch.autograd.Function):
     def backward(ctx, gy):
         x2, wb, pre = ctx.saved_tensors
         g = gy.reshape(-1, gy.shape[-1])
-        if ctx.act == "gelu_tanh":
+        if ctx.act == "gelu_tanh" and pre.dtype == _BF16:
+            g = ops.gelu_tanh_bwd(g, pre)
+        elif ctx.act == "gelu_tanh":
             with torch.enable_grad():
                 p = pre.detach().requires_grad_(True)
                 out = F.gelu(p, approximate="tanh")
                 (g,) = torch.autograd.grad(out, p, g.float())
         gb = g.to(_BF16)
-        # dX = dY·W  → GEMM(dY, Wᵀ) ; dW = dYᵀ·X → GEMM(dYᵀ, Xᵀ)
-        dx = ops.linear(gb, wb.t().contiguous(), None, None, out_dtype=torch.float32)
-        dw = ops.linear(gb.t().contiguous(), x2.t().contiguous(), None, None, out_dtype=torch.float32)
+        # dX = dY·W: W read MN-major in place; dW = dYᵀ·X: dY and X read MN-major in place
+        dx_dtype = _BF16 if ctx.x_dtype == _BF16 else torch.float32
+        dx = ops.gemm_t(gb, wb, a_mn=False, b_mn=True, out_dtype=dx_dtype)
+        if dx is None:
+            dx = ops.linear(gb, wb.t().contiguous(), None, None, out_dtype=torch.float32)
+        dw = ops.gemm_t(gb, x2, a_mn=True, b_mn=True, out_dtype=torch.float32)
+        if dw is None:
+            dw = ops.linear(gb.t().contiguous(), x2.t().contiguous(), None, None, out_dtype=torch.float32)
         db = g.float().sum(0) if ctx.has_b else None
         return dx.view(ctx.in_shape).to(ctx.x_dtype), dw.to(ctx.w_dtype), db, None
+
+
+class _GatedAddFn(torch.autograd.Function):
+    """out = resid + y·gate[b] (fp32 residual, bf16 branch output), fused fwd/bwd kernels."""
+
+    @staticmethod
+    def forward(ctx, resid, y, gate):
+        ctx.save_for_backward(y, gate)
+        ctx.has_gate = gate is not None
+        return ops.gated_add(resid, y, gate)
+
+    @staticmethod
+    def backward(ctx, dout):
+        y, gate = ctx.saved_tensors
+        dout = dout.float().contiguous()
+        if not ctx.has_gate:
+            return dout, dout.to(_BF16), None
+        dy, dgate = ops.gated_add_bwd(dout, y, gate)
+        return dout, dy, dgate.to(gate.dtype)
+
+
+class _LNModFn(torch.autograd.Function):
+    """bf16 LN(x)·(1+scale[b]) + shift[b] of the fp32 residual, fused fwd/bwd kernels."""
+
+    @staticmethod
+    def forward(ctx, x, shift, scale, eps):
+        ctx.save_for_backward(x, scale)
+        ctx.eps = eps
+        return ops.ln_modulate(x, shift, scale, eps)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, scale = ctx.saved_tensors
+        dx, dsc, dsh = ops.ln_modulate_bwd(x, dy, scale, ctx.eps)
+        return dx, dsh, dsc, None
+
+
+class _QKNormRopeFn(torch.autograd.Function):
+    """Full-row RMSNorm of q and k + 3-D RoPE on a fused qkv [B,n,3C] (out of place)."""
+
+    @staticmethod
+    def forward(ctx, qkv, wq, wk, pos, freqs, num_heads, eps):
+        C = qkv.shape[-1] // 3
+        raw = qkv[..., :2 * C].contiguous()
+        out = qkv.contiguous().clone()
+        ops.qk_norm_rope(out, wq, wk, pos, freqs, num_heads, eps)
+        ctx.save_for_backward(raw, wq, wk, pos, freqs)
+        ctx.eps = eps
+        ctx.D = C // num_heads
+        return out
+
+    @staticmethod
+    def backward(ctx, gout):
+        raw, wq, wk, pos, freqs = ctx.saved_tensors
+        C = raw.shape[-1] // 2
+        B, n = raw.shape[:2]
+        H = C // ctx.D
+        sh = (B, n, H, ctx.D)
+        dq, dk, dv = gout[..., :C].reshape(sh), gout[..., C:2 * C].reshape(sh), gout[..., 2 * C:].reshape(sh)
+        dqkv, dwq, dwk = ops.qk_norm_rope_bwd(raw, dq, dk, dv, wq, wk, pos, freqs, ctx.eps)
+        return dqkv, dwq.to(wq.dtype), dwk.to(wk.dtype), None, None, None, None
+
+
+def qkv_norm_rope(x, ws, bs, wq_norm, wk_norm, pos, freqs, num_heads: int, eps: float):
+    """Training path of the self-attention input: one GEMM on the concatenated [3C, C]
+    weight, then the fused q/k RMSNorm + RoPE; returns (q, k, v) [B,n,H,D] bf16."""
+    B, n, _ = x.shape
+    W = torch.cat(ws, 0)
+    b = torch.cat(bs, 0) if all(t is not None for t in bs) else None
+    qkv = _LinearFn.apply(x, W, b, None)
+    out = _QKNormRopeFn.apply(qkv, wq_norm, wk_norm, pos, freqs, num_heads, eps)
+    C = out.shape[-1] // 3
+    D = C // num_heads
+    q, k, v = out.split(C, dim=-1)
+    return q.reshape(B, n, num_heads, D), k.reshape(B, n, num_heads, D), v.reshape(B, n, num_heads, D)
 
 
 def linear(x, w, b=None, act: Optional[str] = None):
@@ -99,6 +186,8 @@ def gated_residual_linear(x, w, b, resid, gate=None):
         out = resid if (resid.dtype == torch.float32 and resid.is_contiguous()) else None
         return ops.linear_gated_residual(x, w, b, resid, gate, out=out)
     y = _LinearFn.apply(x, w, b, None)
+    if resid.dtype == torch.float32 and resid.dim() == 3 and y.shape[-1] % 4 == 0:
+        return _GatedAddFn.apply(resid, y, gate)
     y = y.float()
     return resid.float() + (y * gate.float()[:, None, :] if gate is not None else y)
 
@@ -111,6 +200,8 @@ def ln_modulate(x, shift, scale, eps):
         return y * (1 + scale[:, None, :]) + shift[:, None, :]
     if _fused(x, shift, scale):
         return ops.ln_modulate(x, shift, scale, eps)
+    if x.dtype == torch.float32 and x.dim() == 3 and x.shape[-1] % 4 == 0 and x.shape[-1] <= 8192:
+        return _LNModFn.apply(x.contiguous(), shift.float(), scale.float(), eps)
     y = F.layer_norm(x.float(), (x.shape[-1],), eps=eps)
     return (y * (1 + scale.float()[:, None, :]) + shift.float()[:, None, :]).to(_BF16)
 

@@ -126,6 +126,12 @@ class OSPNextSelfAttention(nn.Module):
             W, b = self.packed_qkv()
             qkv = Fn.ops.linear(x, W, b)
             return Fn.ops.qk_norm_rope(qkv, self.norm_q.weight, self.norm_k.weight, ctx.pos, ctx.freqs, H, self.eps)
+        if (x.is_cuda and self.qk_norm and not lora and not _hif8(self) and ctx.pos is not None
+                and all(type(m) is nn.Linear for m in (self.q, self.k, self.v))):
+            # training: one QKV GEMM + fused q/k norm and RoPE with kernel backward
+            return Fn.qkv_norm_rope(x, (self.q.weight, self.k.weight, self.v.weight),
+                                    (self.q.bias, self.k.bias, self.v.bias), self.norm_q.weight,
+                                    self.norm_k.weight, ctx.pos, ctx.freqs, H, self.eps)
         q = self.norm_q(_lin(self.q, x)).view(B, n, H, D)
         k = self.norm_k(_lin(self.k, x)).view(B, n, H, D)
         v = _lin(self.v, x).view(B, n, H, D)

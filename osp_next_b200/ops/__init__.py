@@ -88,6 +88,21 @@ def linear(x, weight, bias=None, act: Optional[str] = None, out_dtype=_BF16):
     return out.view(*shp[:-1], N)
 
 
+def gemm_t(a, b, a_mn: bool, b_mn: bool, out_dtype=torch.float32):
+    """``A·Bᵀ`` with A = a (or aᵀ when ``a_mn``: a stored [K, M]) and B = b (or bᵀ when
+    ``b_mn``: b stored [K, N]) on the tcgen05 GEMM, reading MN-major operands in place.
+    Returns None when the shapes miss the kernel's alignment rules (rows of a multiple of
+    8 elements, N a multiple of 32) so the caller can fall back."""
+    a, b = _c(a.to(_BF16)), _c(b.to(_BF16))
+    M = a.shape[1] if a_mn else a.shape[0]
+    N = b.shape[1] if b_mn else b.shape[0]
+    if a.shape[1] % 8 or b.shape[1] % 8 or N % 32 or not (a_mn or b_mn):
+        return None
+    out = torch.empty(M, N, dtype=out_dtype, device=a.device)
+    ext().gemm_t(a, b, out, bool(a_mn), bool(b_mn))
+    return out
+
+
 def linear_gated_residual(x, weight, bias, resid, gate=None, dest_row=None, n_out=None, out=None):
     """``resid + (x·Wᵀ+b)·gate`` with fp32 residual, optional row remap on store.
 
@@ -127,6 +142,82 @@ def linear_gated_residual_p2p(x, weight, bias, resid, gate, dest_rank, dest_row,
     ext().gemm_p2p(a, w, None if bias is None else bias.float().contiguous(), _c(resid.float()).view(-1, C),
                    None if gate is None else gate.float().contiguous(), dest_rank, dest_row, out_ptrs, n,
                    int(n_stride))
+
+
+# ----------------------------------------------------------------------------- training-only ops
+# (CUDA only: the autograd wrappers in models/functional.py call them; CPU training uses
+# plain PyTorch autograd)
+
+_ROWS_PER_CTA = 32
+
+
+def _chunks(n: int) -> int:
+    return (n + _ROWS_PER_CTA - 1) // _ROWS_PER_CTA
+
+
+def linear_gelu_aux(x2, w, b):
+    """(gelu_tanh(x·Wᵀ+b), x·Wᵀ+b) both bf16, from one GEMM (FFN-up training forward)."""
+    N = w.shape[0]
+    out = torch.empty(x2.shape[0], N, dtype=_BF16, device=x2.device)
+    aux = torch.empty_like(out)
+    ext().gemm_gelu_aux(_c(x2), _c(w.to(_BF16)), None if b is None else b.float().contiguous(), out, aux)
+    return out, aux
+
+
+def gelu_tanh_bwd(dh, pre):
+    dpre = torch.empty_like(pre)
+    ext().gelu_tanh_bwd(_c(dh.to(_BF16)), _c(pre), dpre)
+    return dpre
+
+
+def ln_modulate_bwd(x, dy, scale, eps: float = 1e-6):
+    """→ (dx fp32, dscale [B,C], dshift [B,C]) for y = LN(x)·(1+scale)+shift, x fp32 [B,n,C]."""
+    B, n, C = x.shape
+    dx = torch.empty_like(x)
+    ps = torch.empty(B, _chunks(n), C, dtype=torch.float32, device=x.device)
+    ph = torch.empty_like(ps)
+    ext().ln_modulate_bwd(_c(x), _c(dy.to(_BF16)), _c(scale.float()), dx, ps, ph, float(eps))
+    return dx, ps.sum(1), ph.sum(1)
+
+
+def gated_add(resid, y, gate=None):
+    """resid + y·gate[b] (fp32 out; resid fp32 [B,n,C], y bf16, gate [B,C] or None)."""
+    out = torch.empty(resid.shape, dtype=torch.float32, device=resid.device)
+    ext().gated_add_fwd(_c(resid.float()), _c(y.to(_BF16)), None if gate is None else _c(gate.float()), out)
+    return out
+
+
+def gated_add_bwd(dout, y, gate):
+    """→ (dy bf16 = dout·gate, dgate [B,C] = Σ_rows dout·y)."""
+    B, n, C = dout.shape
+    dy = torch.empty(dout.shape, dtype=_BF16, device=dout.device)
+    part = torch.empty(B, _chunks(n), C, dtype=torch.float32, device=dout.device)
+    ext().gated_add_bwd(_c(dout.float()), _c(y.to(_BF16)), _c(gate.float()), dy, part)
+    return dy, part.sum(1)
+
+
+def qk_norm_rope_bwd(raw, dq, dk, dv, wq, wk, pos, freqs, eps: float = 1e-6):
+    """Gradient of :func:`qk_norm_rope` w.r.t. the fused qkv [B,n,3C] and the two norm
+    weights; ``raw`` = the pre-norm q|k [B,n,2C] (bf16), dq/dk/dv [B,n,H,D]."""
+    B, n, C2 = raw.shape
+    C = C2 // 2
+    D = dq.shape[-1]
+    dqkv = torch.empty(B, n, 3 * C, dtype=_BF16, device=raw.device)
+    dqkv[..., 2 * C:] = dv.reshape(B, n, C)
+    pos = pos.to(device=raw.device, dtype=torch.int32).contiguous()
+    freqs = freqs.to(device=raw.device, dtype=torch.float32).contiguous()
+    dws = []
+    for part, (g, w) in enumerate(((dq, wq), (dk, wk))):
+        g2 = g.reshape(B * n, C)
+        if g2.dtype not in (_BF16, torch.float32):
+            g2 = g2.float()
+        if g2.stride(-1) != 1 or (g2.stride(0) * g2.element_size()) % 16:
+            g2 = g2.contiguous()
+        dwp = torch.empty(B, _chunks(n), C, dtype=torch.float32, device=raw.device)
+        ext().qk_norm_rope_bwd(raw.reshape(B * n, C2), g2, _c(w.float()), pos, freqs, dqkv.view(B * n, 3 * C), dwp,
+                               part, B, n, C, D, float(eps))
+        dws.append(dwp.sum((0, 1)))
+    return dqkv, dws[0], dws[1]
 
 
 # ----------------------------------------------------------------------------- attention

@@ -10,6 +10,19 @@ namespace osp {
 void gemm(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& bias, at::Tensor& out,
           int64_t act, const c10::optional<at::Tensor>& resid, const c10::optional<at::Tensor>& gate,
           const c10::optional<at::Tensor>& dest_row, int64_t rows_per_batch, int64_t n_out);
+void gemm_t(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, bool b_mn);
+void gemm_gelu_aux(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& bias, at::Tensor& out,
+                   at::Tensor& aux);
+void ln_modulate_bwd(const at::Tensor& x, const at::Tensor& dy, const at::Tensor& scale, at::Tensor& dx,
+                     at::Tensor& dscale_part, at::Tensor& dshift_part, double eps);
+void gated_add_fwd(const at::Tensor& resid, const at::Tensor& y, const c10::optional<at::Tensor>& gate,
+                   at::Tensor& out);
+void gated_add_bwd(const at::Tensor& dout, const at::Tensor& y, const at::Tensor& gate, at::Tensor& dy,
+                   at::Tensor& dgate_part);
+void qk_norm_rope_bwd(const at::Tensor& raw, const at::Tensor& g, const at::Tensor& w, const at::Tensor& pos,
+                      const at::Tensor& freqs, at::Tensor& dqkv, at::Tensor& dw_part, int64_t part, int64_t B,
+                      int64_t n, int64_t C, int64_t D, double eps);
+void gelu_tanh_bwd(const at::Tensor& dh, const at::Tensor& pre, at::Tensor& dpre);
 void ln_modulate(const at::Tensor& x, const c10::optional<at::Tensor>& shift, const c10::optional<at::Tensor>& scale,
                  const c10::optional<at::Tensor>& w, const c10::optional<at::Tensor>& b, at::Tensor& out, double eps);
 void rms_norm(const at::Tensor& x, const c10::optional<at::Tensor>& w, at::Tensor& out, double eps);
@@ -72,6 +85,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ln_modulate", &osp::ln_modulate);
   m.def("rms_norm", &osp::rms_norm);
   m.def("qk_norm_rope", &osp::qk_norm_rope);
+  m.def("gemm_t", &osp::gemm_t);
+  m.def("gemm_gelu_aux", &osp::gemm_gelu_aux);
+  m.def("ln_modulate_bwd", &osp::ln_modulate_bwd);
+  m.def("gated_add_fwd", &osp::gated_add_fwd);
+  m.def("gated_add_bwd", &osp::gated_add_bwd);
+  m.def("qk_norm_rope_bwd", &osp::qk_norm_rope_bwd);
+  m.def("gelu_tanh_bwd", &osp::gelu_tanh_bwd);
   m.def("attention_fwd", &osp::attention_fwd);
   m.def("attention_bwd", &osp::attention_bwd);
   m.def("cfg_euler", &osp::cfg_euler);

@@ -143,11 +143,12 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                :: "r"(smem_u32(bar)) : "memory");
 }
 
-// Instruction descriptor: bf16 × bf16 → fp32, A K-major, B K-major unless b_mn_major.
-__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool b_mn_major = false) {
+// Instruction descriptor: bf16 × bf16 → fp32; A / B K-major unless a_mn_major / b_mn_major.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool b_mn_major = false, bool a_mn_major = false) {
   return (1u << 4)                               // D format: f32
        | (1u << 7)                               // A format: bf16
        | (1u << 10)                              // B format: bf16
+       | ((a_mn_major ? 1u : 0u) << 15)          // A major
        | ((b_mn_major ? 1u : 0u) << 16)          // B major
        | ((uint32_t)(N >> 3) << 17)
        | ((uint32_t)(M >> 4) << 24);

@@ -14,6 +14,9 @@
 //   warps 2..5  epilogue:    tcgen05.ld 32 columns at a time, bias / GELU-tanh /
 //               gated fp32 residual (+ row remap = fused layout change), global store
 // Tiles are visited in M-groups of 16 so the weight stays L2-resident across a group.
+// Either operand may instead be MN-major (stored [K, M] / [K, N], MN contiguous): the
+// backward GEMMs dX = dY·W and dW = dYᵀ·X read dY, W and X in place, with no transposed
+// copies.  An MN-major tile is MN/64 TMA boxes of 64 K-rows × 64 elements (128B swizzle).
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -42,6 +45,7 @@ struct GemmArgs {
   int n_out;                // rows per batch of out (residual mode with dest_row)
   const int64_t* out_ptrs;  // [world] peer output buffers (fused SSP exchange) or null
   const int* dest_rank;     // [rows_per_batch] owner rank of each row in the next layout
+  __nv_bfloat16* aux;       // [M, N] bf16 pre-activation (store mode with GELU, training) or null
   int* err;
 };
 
@@ -61,14 +65,15 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
   return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
 }
 
-template <int BN, int MODE, typename OutT>
+template <int BN, int MODE, typename OutT, bool A_MN = false, bool B_MN = false>
 __global__ void __launch_bounds__(192, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
   constexpr int STAGES = kSmemBudget / (kBM * kBK * 2 + BN * kBK * 2);
   constexpr uint32_t A_BYTES = kBM * kBK * 2;
   constexpr uint32_t B_BYTES = BN * kBK * 2;
+  constexpr uint32_t MN_BOX = 64 * kBK * 2;        // one MN-major box: 64 K-rows × 128 B
   constexpr uint32_t TMEM_COLS = 2 * BN;
-  constexpr uint32_t IDESC = idesc_bf16(kBM, BN);
+  constexpr uint32_t IDESC = idesc_bf16(kBM, BN, B_MN, A_MN);
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base_u32 = smem_u32(smem_raw);
@@ -119,8 +124,20 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, args.err, kErrGemmProducer)) { *abort_flag = 1; break; }
           mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
-          tma_load_2d(&tmA, &full[stage], sA + stage * A_BYTES, kb * kBK, mb * kBM);
-          tma_load_2d(&tmB, &full[stage], sB + stage * B_BYTES, kb * kBK, nb * BN);
+          if constexpr (A_MN) {
+#pragma unroll
+            for (int c = 0; c < kBM / 64; ++c)
+              tma_load_2d(&tmA, &full[stage], sA + stage * A_BYTES + c * MN_BOX, mb * kBM + 64 * c, kb * kBK);
+          } else {
+            tma_load_2d(&tmA, &full[stage], sA + stage * A_BYTES, kb * kBK, mb * kBM);
+          }
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c)
+              tma_load_2d(&tmB, &full[stage], sB + stage * B_BYTES + c * MN_BOX, nb * BN + 64 * c, kb * kBK);
+          } else {
+            tma_load_2d(&tmB, &full[stage], sB + stage * B_BYTES, kb * kBK, nb * BN);
+          }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
@@ -145,8 +162,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
-            const uint64_t ad = sdesc_sw128(a_addr + k * 32, 16, 1024);
-            const uint64_t bd = sdesc_sw128(b_addr + k * 32, 16, 1024);
+            // K-major: +32 B per 16-wide K step; MN-major: +16 rows × 128 B, boxes MN_BOX apart
+            const uint64_t ad = A_MN ? sdesc_sw128(a_addr + k * 2048, MN_BOX, 1024)
+                                     : sdesc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(b_addr + k * 2048, MN_BOX, 1024)
+                                     : sdesc_sw128(b_addr + k * 32, 16, 1024);
             umma_bf16(d_tmem, ad, bd, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
@@ -208,6 +228,18 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           }
         }
         if (MODE == kEpiStore) {
+          if (args.aux) {              // pre-activation kept for the GELU backward
+            uint4* a4 = reinterpret_cast<uint4*>(args.aux + out_row * args.N + col0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint4 w;
+              w.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+              w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+              w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+              w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+              a4[j] = w;
+            }
+          }
           if (args.act == 1) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_f(v[j]);
@@ -273,11 +305,15 @@ static int num_sms(int dev) {
   return cache[dev];
 }
 
-template <int BN, int MODE, typename OutT>
+template <int BN, int MODE, typename OutT, bool A_MN = false, bool B_MN = false>
 static void launch_gemm(const at::Tensor& a, const at::Tensor& b, GemmArgs& args, cudaStream_t stream) {
-  CUtensorMap tmA = make_tmap_2d_bf16(a.data_ptr(), args.K, args.M, a.stride(0), kBK, kBM);
-  CUtensorMap tmB = make_tmap_2d_bf16(b.data_ptr(), args.K, args.N, b.stride(0), kBK, BN);
-  auto kern = gemm_kernel<BN, MODE, OutT>;
+  // K-major operand: rows of K elements (box 64 K × tile rows); MN-major: rows of M/N
+  // elements, one row per K index (box 64 MN × 64 K)
+  CUtensorMap tmA = A_MN ? make_tmap_2d_bf16(a.data_ptr(), args.M, args.K, a.stride(0), 64, kBK)
+                         : make_tmap_2d_bf16(a.data_ptr(), args.K, args.M, a.stride(0), kBK, kBM);
+  CUtensorMap tmB = B_MN ? make_tmap_2d_bf16(b.data_ptr(), args.N, args.K, b.stride(0), 64, kBK)
+                         : make_tmap_2d_bf16(b.data_ptr(), args.K, args.N, b.stride(0), kBK, BN);
+  auto kern = gemm_kernel<BN, MODE, OutT, A_MN, B_MN>;
   constexpr int smem = gemm_smem_bytes<BN>();
   static bool configured = false;
   if (!configured) {
@@ -358,6 +394,80 @@ void gemm(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tens
     if (args.N % 256 == 0) launch_gemm<256, kEpiStore, float>(a, b, args, stream);
     else if (args.N % 128 == 0) launch_gemm<128, kEpiStore, float>(a, b, args, stream);
     else launch_gemm<64, kEpiStore, float>(a, b, args, stream);
+  }
+}
+
+// Training forward of FFN-up: out = gelu_tanh(a·bᵀ + bias) and aux = a·bᵀ + bias (both bf16).
+void gemm_gelu_aux(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& bias, at::Tensor& out,
+                   at::Tensor& aux) {
+  TORCH_CHECK(aux.is_cuda() && aux.scalar_type() == at::kBFloat16 && aux.is_contiguous() &&
+              out.scalar_type() == at::kBFloat16 && aux.sizes() == out.sizes(), "gemm_gelu_aux: bf16 out/aux");
+  TORCH_CHECK(a.is_cuda() && a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 && a.dim() == 2 &&
+              b.dim() == 2 && a.size(1) == b.size(1) && a.stride(1) == 1 && b.stride(1) == 1 &&
+              a.size(1) % 8 == 0 && b.size(0) % 32 == 0 && out.is_contiguous() &&
+              out.numel() == a.size(0) * b.size(0), "gemm_gelu_aux: bf16 K-contiguous operands, N % 32, K % 8");
+  TORCH_CHECK((a.stride(0) * 2) % 16 == 0 && (b.stride(0) * 2) % 16 == 0, "gemm_gelu_aux: row strides 16-byte aligned");
+  c10::cuda::CUDAGuard guard(a.device());
+  GemmArgs args{};
+  args.M = (int)a.size(0);
+  args.N = (int)b.size(0);
+  args.K = (int)a.size(1);
+  args.bias = bias.has_value() ? bias->data_ptr<float>() : nullptr;
+  if (bias.has_value()) TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->numel() == args.N, "gemm_gelu_aux: bias");
+  args.act = 1;
+  args.out = out.data_ptr();
+  args.aux = reinterpret_cast<__nv_bfloat16*>(aux.data_ptr());
+  args.err = error_word(a.get_device());
+  if (args.M == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (args.N % 256 == 0) launch_gemm<256, kEpiStore, __nv_bfloat16>(a, b, args, stream);
+  else if (args.N % 128 == 0) launch_gemm<128, kEpiStore, __nv_bfloat16>(a, b, args, stream);
+  else launch_gemm<64, kEpiStore, __nv_bfloat16>(a, b, args, stream);
+}
+
+template <bool A_MN, bool B_MN, typename OutT>
+static void launch_gemm_t(const at::Tensor& a, const at::Tensor& b, GemmArgs& args, cudaStream_t stream) {
+  if (args.N % 256 == 0) launch_gemm<256, kEpiStore, OutT, A_MN, B_MN>(a, b, args, stream);
+  else if (args.N % 128 == 0) launch_gemm<128, kEpiStore, OutT, A_MN, B_MN>(a, b, args, stream);
+  else launch_gemm<64, kEpiStore, OutT, A_MN, B_MN>(a, b, args, stream);
+}
+
+// out[M,N] = A·Bᵀ with A given as a [M,K] (a_mn: stored [K,M]) and B as b [N,K]
+// (b_mn: stored [K,N]); the backward-pass GEMMs.  No bias / epilogue op.
+void gemm_t(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, bool b_mn) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "gemm_t: CUDA tensors expected");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm_t: bf16 operands");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1, "gemm_t: 2-D row-major operands");
+  const int64_t M = a_mn ? a.size(1) : a.size(0), K = a_mn ? a.size(0) : a.size(1);
+  const int64_t N = b_mn ? b.size(1) : b.size(0), Kb = b_mn ? b.size(0) : b.size(1);
+  TORCH_CHECK(K == Kb, "gemm_t: contraction sizes differ");
+  TORCH_CHECK(a.size(1) % 8 == 0 && b.size(1) % 8 == 0, "gemm_t: rows must be a multiple of 8 elements (16 B)");
+  TORCH_CHECK((a.stride(0) * 2) % 16 == 0 && (b.stride(0) * 2) % 16 == 0, "gemm_t: row strides 16-byte aligned");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(a.data_ptr()) % 16 == 0 &&
+              reinterpret_cast<uintptr_t>(b.data_ptr()) % 16 == 0, "gemm_t: 16-byte aligned operands");
+  TORCH_CHECK(N % 32 == 0, "gemm_t: N must be a multiple of 32");
+  TORCH_CHECK(out.is_contiguous() && out.numel() == M * N, "gemm_t: contiguous out [M,N]");
+  TORCH_CHECK(a_mn || b_mn, "gemm_t: use gemm for two K-major operands");
+  c10::cuda::CUDAGuard guard(a.device());
+  GemmArgs args{};
+  args.M = (int)M;
+  args.N = (int)N;
+  args.K = (int)K;
+  args.out = out.data_ptr();
+  args.err = error_word(a.get_device());
+  if (M == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const bool f32 = out.scalar_type() == at::kFloat;
+  TORCH_CHECK(f32 || out.scalar_type() == at::kBFloat16, "gemm_t: out bf16 or f32");
+  if (a_mn && b_mn) {
+    if (f32) launch_gemm_t<true, true, float>(a, b, args, stream);
+    else launch_gemm_t<true, true, __nv_bfloat16>(a, b, args, stream);
+  } else if (b_mn) {
+    if (f32) launch_gemm_t<false, true, float>(a, b, args, stream);
+    else launch_gemm_t<false, true, __nv_bfloat16>(a, b, args, stream);
+  } else {
+    if (f32) launch_gemm_t<true, false, float>(a, b, args, stream);
+    else launch_gemm_t<true, false, __nv_bfloat16>(a, b, args, stream);
   }
 }
 

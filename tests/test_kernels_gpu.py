@@ -332,3 +332,111 @@ def test_model_training_gradients_match_cpu_fp32():
             bad.append((n, rel))
     assert not bad, bad
     _no_device_error()
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, True), (True, True), (True, False)])
+@pytest.mark.parametrize("M,N,K", [(300, 160, 200), (1024, 512, 4096), (128, 96, 77)])
+def test_gemm_mn_major_operands(a_mn, b_mn, M, N, K):
+    """GEMM with operands read MN-major in place (the backward-pass layouts) vs fp32."""
+    torch.manual_seed(13)
+    if a_mn and M % 8:
+        pytest.skip("MN-major A needs M % 8 == 0")
+    A = torch.randn(M, K, device=DEV).to(torch.bfloat16)
+    Bm = torch.randn(N, K, device=DEV).to(torch.bfloat16)
+    a = A.t().contiguous() if a_mn else A
+    b = Bm.t().contiguous() if b_mn else Bm
+    if a.shape[1] % 8 or b.shape[1] % 8:
+        pytest.skip("rows must be a multiple of 8 elements")
+    got = ops.gemm_t(a, b, a_mn, b_mn)
+    exp = A.float() @ Bm.float().t()
+    _close(got, exp, 2e-3, 2e-3 * K ** 0.5)
+    _no_device_error()
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
+
+
+def test_training_ln_modulate_and_gated_add_grads():
+    """Fused LN+modulate and gated-residual autograd functions vs fp32 PyTorch autograd."""
+    from osp_next_b200.models import functional as Fn
+    torch.manual_seed(21)
+    B, n, C = 2, 301, 1536
+    x = torch.randn(B, n, C, device=DEV, requires_grad=True)
+    sh = (torch.randn(B, C, device=DEV) * 0.1).requires_grad_(True)
+    sc = (torch.randn(B, C, device=DEV) * 0.1).requires_grad_(True)
+    g = torch.randn(B, n, C, device=DEV)
+    y = Fn._LNModFn.apply(x, sh, sc, 1e-6)
+    (y.float() * g).sum().backward()
+    got = (x.grad.clone(), sh.grad.clone(), sc.grad.clone())
+    for t in (x, sh, sc):
+        t.grad = None
+    yr = torch.nn.functional.layer_norm(x, (C,), eps=1e-6) * (1 + sc[:, None]) + sh[:, None]
+    (yr.to(torch.bfloat16).float() * g).sum().backward()
+    for a, b in zip(got, (x.grad, sh.grad, sc.grad)):
+        assert _rel(a, b) < 1e-2
+    # gated residual add
+    r = torch.randn(B, n, C, device=DEV, requires_grad=True)
+    v = torch.randn(B, n, C, device=DEV).to(torch.bfloat16).requires_grad_(True)
+    gate = torch.randn(B, C, device=DEV, requires_grad=True)
+    out = Fn._GatedAddFn.apply(r, v, gate)
+    exp = r + v.float() * gate[:, None]
+    _close(out, exp.detach(), 1e-6, 1e-6)
+    (out * g).sum().backward()
+    got = (r.grad.clone(), v.grad.clone(), gate.grad.clone())
+    for t in (r, v, gate):
+        t.grad = None
+    (exp * g).sum().backward()
+    for a, b in zip(got, (r.grad, v.grad, gate.grad)):
+        assert _rel(a, b) < 1e-2
+    _no_device_error()
+
+
+def test_training_qk_norm_rope_grads():
+    """Fused q/k RMSNorm + RoPE autograd function vs the fp32 reference under autograd."""
+    from osp_next_b200.models import functional as Fn
+    torch.manual_seed(22)
+    B, n, H, D = 2, 150, 4, 128
+    C = H * D
+    qkv = torch.randn(B, n, 3 * C, device=DEV).to(torch.bfloat16).requires_grad_(True)
+    wq = (1 + 0.1 * torch.randn(C, device=DEV)).requires_grad_(True)
+    wk = (1 + 0.1 * torch.randn(C, device=DEV)).requires_grad_(True)
+    pos = torch.stack([torch.arange(n) // 30, (torch.arange(n) // 6) % 5, torch.arange(n) % 6], 1).int()
+    freqs = ref.rope_freqs(D).to(DEV)
+    out = Fn._QKNormRopeFn.apply(qkv, wq, wk, pos.to(DEV), freqs, H, 1e-6)
+    g = torch.randn(B, n, 3 * C, device=DEV)
+    (out.float() * g).sum().backward()
+    got = (qkv.grad.clone(), wq.grad.clone(), wk.grad.clone())
+    for t in (qkv, wq, wk):
+        t.grad = None
+    x = qkv.float()
+    q, k, v = x.split(C, dim=-1)
+
+    def nr(t, w):
+        t = t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + 1e-6) * w
+        return ref.apply_rope(t.view(B, n, H, D), pos.to(DEV), freqs).reshape(B, n, C)
+    exp = torch.cat([nr(q, wq), nr(k, wk), v], -1)
+    (exp * g).sum().backward()
+    for a, b in zip(got, (qkv.grad, wq.grad, wk.grad)):
+        assert _rel(a, b) < 2e-2, _rel(a, b)
+    _no_device_error()
+
+
+def test_training_gelu_linear_grads():
+    from osp_next_b200.models import functional as Fn
+    torch.manual_seed(23)
+    x = torch.randn(2, 200, 512, device=DEV).requires_grad_(True)
+    w = (torch.randn(1024, 512, device=DEV) / 512 ** 0.5).requires_grad_(True)
+    b = torch.randn(1024, device=DEV).requires_grad_(True)
+    y = Fn._LinearFn.apply(x, w, b, "gelu_tanh")
+    g = torch.randn_like(y, dtype=torch.float32)
+    (y.float() * g).sum().backward()
+    got = (x.grad.clone(), w.grad.clone(), b.grad.clone())
+    for t in (x, w, b):
+        t.grad = None
+    yr = torch.nn.functional.gelu(x.to(torch.bfloat16).float() @ w.to(torch.bfloat16).float().t() + b,
+                                  approximate="tanh")
+    (yr * g).sum().backward()
+    for a, e in zip(got, (x.grad, w.grad, b.grad)):
+        assert _rel(a, e) < 2e-2, _rel(a, e)
+    _no_device_error()

@@ -52,7 +52,10 @@ def _sp_broadcast(tensors, group):
     return tensors
 
 
-def main(config):
+def main(config, on_step=None):
+    """Train per ``config``.  ``on_step(it, step_ms, tokens_per_step)`` (optional) is called on
+    every rank after each optimizer step, once the step's device work has finished.
+    Returns the per-step device times (ms, CUDA events on this rank)."""
     logger = get_logger()
     setup_distributed_env(timeout_s=config.get("timeout_s", 600))
     rank, W = B.rank(), B.world()
@@ -171,6 +174,8 @@ def main(config):
             torch.cuda.synchronize()
             ms = ev0.elapsed_time(ev1)
             step_times.append(ms)
+            if on_step is not None:
+                on_step(it, ms, tokens_per_step)
         if it % log_interval == 0:
             lv = gather_data_from_all_ranks(loss.detach().float() * accum).mean().item()
             ms_max = step_times[-1] if step_times else 0.0
