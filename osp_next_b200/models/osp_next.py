@@ -56,7 +56,12 @@ class WanRMSNorm(nn.Module):
         self.eps = eps
         self.weight = nn.Parameter(torch.ones(dim))
 
-    def forward(self, x):
+    def forward(self, x, weight_only: bool = False):
+        if weight_only:
+            # the weight as a differentiable tensor produced inside this module's forward:
+            # under FSDP the module's own hooks gather the parameter for the call and reduce
+            # its gradient afterwards, so a fused kernel elsewhere can consume it
+            return self.weight * 1.0
         return Fn.rms_norm(x, self.weight, self.eps)
 
     def reset_parameters(self):
@@ -130,8 +135,8 @@ class OSPNextSelfAttention(nn.Module):
                 and all(type(m) is nn.Linear for m in (self.q, self.k, self.v))):
             # training: one QKV GEMM + fused q/k norm and RoPE with kernel backward
             return Fn.qkv_norm_rope(x, (self.q.weight, self.k.weight, self.v.weight),
-                                    (self.q.bias, self.k.bias, self.v.bias), self.norm_q.weight,
-                                    self.norm_k.weight, ctx.pos, ctx.freqs, H, self.eps)
+                                    (self.q.bias, self.k.bias, self.v.bias), self.norm_q(None, weight_only=True),
+                                    self.norm_k(None, weight_only=True), ctx.pos, ctx.freqs, H, self.eps)
         q = self.norm_q(_lin(self.q, x)).view(B, n, H, D)
         k = self.norm_k(_lin(self.k, x)).view(B, n, H, D)
         v = _lin(self.v, x).view(B, n, H, D)
