@@ -205,7 +205,7 @@ def qk_norm_rope_bwd(raw, dq, dk, dv, wq, wk, pos, freqs, eps: float = 1e-6):
     dqkv = torch.empty(B, n, 3 * C, dtype=_BF16, device=raw.device)
     dqkv[..., 2 * C:] = dv.reshape(B, n, C)
     pos = pos.to(device=raw.device, dtype=torch.int32).contiguous()
-    freqs = freqs.to(device=raw.device, dtype=torch.float32).contiguous()
+    cs = rope_cos_sin(freqs, raw.device)
     dws = []
     for part, (g, w) in enumerate(((dq, wq), (dk, wk))):
         g2 = g.reshape(B * n, C)
@@ -214,13 +214,31 @@ def qk_norm_rope_bwd(raw, dq, dk, dv, wq, wk, pos, freqs, eps: float = 1e-6):
         if g2.stride(-1) != 1 or (g2.stride(0) * g2.element_size()) % 16:
             g2 = g2.contiguous()
         dwp = torch.empty(B, _chunks(n), C, dtype=torch.float32, device=raw.device)
-        ext().qk_norm_rope_bwd(raw.reshape(B * n, C2), g2, _c(w.float()), pos, freqs, dqkv.view(B * n, 3 * C), dwp,
+        ext().qk_norm_rope_bwd(raw.reshape(B * n, C2), g2, _c(w.float()), pos, cs, dqkv.view(B * n, 3 * C), dwp,
                                part, B, n, C, D, float(eps))
         dws.append(dwp.sum((0, 1)))
     return dqkv, dws[0], dws[1]
 
 
 # ----------------------------------------------------------------------------- attention
+
+_CS_CACHE = {}
+
+
+def rope_cos_sin(freqs: torch.Tensor, device) -> torch.Tensor:
+    """(cos, sin) table [L, D/2, 2] fp32 of an angle table, evaluated in fp64 once per
+    table (cached), so the kernels rotate with table loads instead of sincos."""
+    key = (freqs.data_ptr(), freqs._version, tuple(freqs.shape), str(device))
+    hit = _CS_CACHE.get(key)
+    if hit is not None and hit[0] is freqs:
+        return hit[1]
+    a = freqs.to(device=device, dtype=torch.float64)
+    cs = torch.stack([a.cos(), a.sin()], -1).float().contiguous()
+    if len(_CS_CACHE) > 16:
+        _CS_CACHE.clear()
+    _CS_CACHE[key] = (freqs, cs)
+    return cs
+
 
 def qk_norm_rope(qkv, wq, wk, pos, freqs, num_heads: int, eps: float = 1e-6):
     """Fused full-row RMSNorm(q), RMSNorm(k) and 3-D RoPE on a fused qkv buffer.
@@ -235,7 +253,7 @@ def qk_norm_rope(qkv, wq, wk, pos, freqs, num_heads: int, eps: float = 1e-6):
     D = C // num_heads
     ext().qk_norm_rope(qkv, wq.float().contiguous(), wk.float().contiguous(),
                        pos.to(device=qkv.device, dtype=torch.int32).contiguous(),
-                       freqs.to(device=qkv.device, dtype=torch.float32).contiguous(), num_heads, float(eps))
+                       rope_cos_sin(freqs, qkv.device), num_heads, float(eps))
     q, k, v = qkv.split(C, dim=-1)
     return q.view(B, n, num_heads, D), k.view(B, n, num_heads, D), v.view(B, n, num_heads, D)
 

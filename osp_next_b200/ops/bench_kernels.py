@@ -17,7 +17,7 @@ import statistics
 
 import torch
 
-from . import attention, attention_bwd, linear, linear_gated_residual, ln_modulate, qk_norm_rope
+from . import attention, attention_bwd, gemm_t, linear, linear_gated_residual, ln_modulate, qk_norm_rope
 from .reference import rope_freqs
 
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
@@ -95,6 +95,22 @@ def cases(size: str):
             return (lambda: attention(q, k, v, sq, sk)), fl, (q.numel() * 4 + k.numel() * 4) * 2
         return setup
 
+    def gemm_bwd(kind, n_out, k_in):
+        # backward GEMMs of a Linear with M tokens: dX = dY·W (W read MN-major),
+        # dW = dYᵀ·X (dY and X read MN-major), fp32 dW
+        def setup():
+            dy = torch.randn(M, n_out, device=dev, dtype=bf)
+            if kind == "dx":
+                w = torch.randn(n_out, k_in, device=dev, dtype=bf)
+                fn = lambda: gemm_t(dy, w, False, True, out_dtype=bf)
+                byts = (M * n_out + n_out * k_in + M * k_in) * 2
+            else:
+                x = torch.randn(M, k_in, device=dev, dtype=bf)
+                fn = lambda: gemm_t(dy, x, True, True)
+                byts = (M * n_out + M * k_in) * 2 + n_out * k_in * 4
+            return fn, 2.0 * M * n_out * k_in, byts
+        return setup
+
     def attn_bwd(lengths):
         # algorithmic FLOPs of the backward: 5 matmuls of 2·L²·D per head (S, dP, dV, dK, dQ)
         def setup():
@@ -130,6 +146,8 @@ def cases(size: str):
         "attn_sparse": attn([G, G, G, G]),
         "attn_dense": attn([N]),
         "attn_cross": attn([N], nk=512),
+        "gemm_ffn_down_bwd_dx": gemm_bwd("dx", C, F),
+        "gemm_ffn_down_bwd_dw": gemm_bwd("dw", C, F),
         "attn_sparse_bwd": attn_bwd([G, G, G, G]),
         "attn_dense_bwd": attn_bwd([N]),
         "ln_modulate": lnmod,

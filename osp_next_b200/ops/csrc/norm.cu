@@ -6,7 +6,8 @@
 //   rms_norm      bf16 out = x·rsqrt(mean(x²)+eps)·w            (want2v.py:77-93)
 //   qk_norm_rope  in place on fused qkv [rows, 3C]: full-row RMSNorm of q and k
 //                 (over all heads, as the reference) then interleaved-pair 3-D RoPE
-//                 with each token's true (t,h,w) (osp_next.py:550-644, 742-752)
+//                 with each token's true (t,h,w) (osp_next.py:550-644, 742-752); the
+//                 rotation reads a precomputed (cos, sin) table instead of evaluating sincos
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -145,7 +146,7 @@ rms_norm_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w
 template <int MAXV>
 __global__ void __launch_bounds__(kRowThreads)
 qk_norm_rope_kernel(__nv_bfloat16* __restrict__ qkv, const float* __restrict__ wq, const float* __restrict__ wk,
-                    const int* __restrict__ pos, const float* __restrict__ freqs, int C, int D, int rows_per_batch,
+                    const int* __restrict__ pos, const float2* __restrict__ cstab, int C, int D, int rows_per_batch,
                     float eps) {
   __shared__ float red[kRowThreads / 32];
   const long row = blockIdx.x;
@@ -184,9 +185,8 @@ qk_norm_rope_kernel(__nv_bfloat16* __restrict__ qkv, const float* __restrict__ w
       for (int p = 0; p < 2; ++p) {
         const int j = ((e % D) >> 1) + p;             // pair index inside the head
         const int prow = j < ct ? pt : (j < ct + ch ? ph : pw);
-        const float ang = freqs[(long)prow * half + j];
-        float sn, cs;
-        sincosf(ang, &sn, &cs);
+        const float2 t = cstab[(long)prow * half + j];      // (cos, sin) of the angle
+        const float cs = t.x, sn = t.y;
         const float q1 = qa[2 * p], q2 = qa[2 * p + 1];
         qa[2 * p] = q1 * cs - q2 * sn;
         qa[2 * p + 1] = q1 * sn + q2 * cs;
@@ -211,6 +211,7 @@ qk_norm_rope_kernel(__nv_bfloat16* __restrict__ qkv, const float* __restrict__ w
     if (nvec <= 1) { constexpr int MV = 1; __VA_ARGS__; }                  \
     else if (nvec <= 2) { constexpr int MV = 2; __VA_ARGS__; }             \
     else if (nvec <= 4) { constexpr int MV = 4; __VA_ARGS__; }             \
+    else if (nvec <= 5) { constexpr int MV = 5; __VA_ARGS__; }             \
     else if (nvec <= 8) { constexpr int MV = 8; __VA_ARGS__; }             \
     else TORCH_CHECK(false, "row too long: C=", C);                        \
   } while (0)
@@ -272,7 +273,8 @@ void qk_norm_rope(at::Tensor& qkv, const at::Tensor& wq, const at::Tensor& wk, c
   TORCH_CHECK(C % 4 == 0 && D % 4 == 0, "qk_norm_rope: C, D multiples of 4");
   const int n = (int)qkv.size(1);
   TORCH_CHECK(pos.scalar_type() == at::kInt && pos.numel() == 3L * n, "qk_norm_rope: pos int32 [n,3]");
-  TORCH_CHECK(freqs.scalar_type() == at::kFloat && freqs.size(1) == D / 2, "qk_norm_rope: freqs f32 [L, D/2]");
+  TORCH_CHECK(freqs.scalar_type() == at::kFloat && freqs.is_contiguous() && freqs.dim() == 3 && freqs.size(1) == D / 2 &&
+              freqs.size(2) == 2, "qk_norm_rope: (cos, sin) table f32 [L, D/2, 2]");
   TORCH_CHECK(wq.scalar_type() == at::kFloat && wk.scalar_type() == at::kFloat, "qk_norm_rope: f32 weights");
   const long rows = qkv.size(0) * (long)n;
   c10::cuda::CUDAGuard guard(qkv.device());
@@ -280,7 +282,7 @@ void qk_norm_rope(at::Tensor& qkv, const at::Tensor& wq, const at::Tensor& wk, c
   if (rows == 0) return;
   OSP_ROW_DISPATCH(C, (qk_norm_rope_kernel<MV><<<rows, kRowThreads, 0, stream>>>(
                           reinterpret_cast<__nv_bfloat16*>(qkv.data_ptr()), wq.data_ptr<float>(),
-                          wk.data_ptr<float>(), pos.data_ptr<int>(), freqs.data_ptr<float>(), C, D, n,
+                          wk.data_ptr<float>(), pos.data_ptr<int>(), reinterpret_cast<const float2*>(freqs.data_ptr<float>()), C, D, n,
                           (float)eps)));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -207,7 +207,7 @@ gated_add_bwd_kernel(const float* __restrict__ dout, const __nv_bfloat16* __rest
 template <int MAXV, typename GT>
 __global__ void __launch_bounds__(kThreads)
 qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ raw, int ld_raw, const GT* __restrict__ g, int ld_g,
-                        const float* __restrict__ w, const int* __restrict__ pos, const float* __restrict__ freqs,
+                        const float* __restrict__ w, const int* __restrict__ pos, const float2* __restrict__ cstab,
                         __nv_bfloat16* __restrict__ dx, int ld_dx, float* __restrict__ dw_part, int part, int n,
                         int C, int D, float eps) {
   __shared__ float2 red[kThreads / 32];
@@ -253,8 +253,8 @@ qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ raw, int ld_raw, const
         for (int p = 0; p < 2; ++p) {
           const int j = ((e % D) >> 1) + p;
           const int prow = j < ct ? pt : (j < ct + ch ? ph : pw);
-          float sn, cs;
-          sincosf(freqs[(long)prow * half + j], &sn, &cs);
+          const float2 t = cstab[(long)prow * half + j];
+          const float cs = t.x, sn = t.y;
           const float g1 = gv[2 * p], g2 = gv[2 * p + 1];
           gv[2 * p] = g1 * cs + g2 * sn;                    // rotateᵀ
           gv[2 * p + 1] = -g1 * sn + g2 * cs;
@@ -398,7 +398,8 @@ void qk_norm_rope_bwd(const at::Tensor& raw, const at::Tensor& g, const at::Tens
               "qk_norm_rope_bwd: g bf16/fp32 with contiguous rows");
   TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous() && w.numel() == C, "qk_norm_rope_bwd: w fp32 [C]");
   TORCH_CHECK(pos.scalar_type() == at::kInt && pos.is_contiguous() && pos.numel() == 3 * n, "qk_norm_rope_bwd: pos");
-  TORCH_CHECK(freqs.scalar_type() == at::kFloat && freqs.is_contiguous(), "qk_norm_rope_bwd: freqs fp32");
+  TORCH_CHECK(freqs.scalar_type() == at::kFloat && freqs.is_contiguous() && freqs.dim() == 3 && freqs.size(2) == 2,
+              "qk_norm_rope_bwd: (cos, sin) table f32 [L, D/2, 2]");
   TORCH_CHECK(C % 4 == 0 && D % 4 == 0 && dw_part.numel() == B * chunks((int)n) * C, "qk_norm_rope_bwd: shapes");
   c10::cuda::CUDAGuard guard(raw.device());
   if (n == 0 || B == 0) return;
@@ -410,12 +411,13 @@ void qk_norm_rope_bwd(const at::Tensor& raw, const at::Tensor& g, const at::Tens
   if (g.scalar_type() == at::kBFloat16) {
     OSP_TRN_DISPATCH((int)C, (trn::qk_norm_rope_bwd_kernel<MV, __nv_bfloat16><<<grid, trn::kThreads, 0, st>>>(
                                  rp, ld_raw, reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), ld_g,
-                                 w.data_ptr<float>(), pos.data_ptr<int>(), freqs.data_ptr<float>(), dp, ld_dx,
+                                 w.data_ptr<float>(), pos.data_ptr<int>(), reinterpret_cast<const float2*>(freqs.data_ptr<float>()), dp, ld_dx,
                                  dw_part.data_ptr<float>(), (int)part, (int)n, (int)C, (int)D, (float)eps)));
   } else {
     OSP_TRN_DISPATCH((int)C, (trn::qk_norm_rope_bwd_kernel<MV, float><<<grid, trn::kThreads, 0, st>>>(
                                  rp, ld_raw, g.data_ptr<float>(), ld_g, w.data_ptr<float>(), pos.data_ptr<int>(),
-                                 freqs.data_ptr<float>(), dp, ld_dx, dw_part.data_ptr<float>(), (int)part, (int)n,
+                                 reinterpret_cast<const float2*>(freqs.data_ptr<float>()), dp, ld_dx,
+                                 dw_part.data_ptr<float>(), (int)part, (int)n,
                                  (int)C, (int)D, (float)eps)));
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
