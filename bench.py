@@ -65,6 +65,9 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--mode", choices=["infer", "train"], default="infer",
                    help="infer: the sec/video headline; train: flow-matching training tokens/s")
+    p.add_argument("--quant", choices=["none", "hif8"], default="none",
+                   help="train mode: HiF8 fake-quant linears (BASELINE config 4) or plain bf16")
+    p.add_argument("--loss-log", default=None, help="train mode: append per-step losses (JSONL) here")
     p.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                    help="SSP layout exchange: fused GEMM-epilogue stores over NVLink, or NCCL all_to_all")
     return p.parse_args()
@@ -277,6 +280,10 @@ def train_config(args, world, out_dir):
                weight_dtype="bf16", gradient_checkpointing=True, seed=1024)
     cfg["model_config"] = dict(cfg.get("model_config", {}), **{k: v for k, v in PRESETS[args.model].items()})
     cfg["model_config"].pop("pretrained_model_dir_or_checkpoint", None)
+    if getattr(args, "quant", "none") == "hif8":
+        cfg["model_config"].update(quant="hif8")
+    if getattr(args, "loss_log", None):
+        cfg["metrics_file"] = args.loss_log
     dc = dict(cfg.get("data_config", {}))
     dc.update(dataset_name="t2v_random_latent", num_workers=2, pin_memory=True, batch_size=1,
               dataset_config=dict(sample_height=args.height, sample_width=args.width,
@@ -325,7 +332,8 @@ def run_train(args, rank, world, local, impl):
     tok = rec[-1][1]
     wall = max_over_ranks((rec[-1][2] - t_first[0]) / len(rec))
     fsdp, ssp = train_layout(world)
-    return {"metric": f"train tokens/s OSP-Next-{args.model} flow matching {args.frames}f "
+    q = "" if args.quant == "none" else f" {args.quant}"
+    return {"metric": f"train tokens/s OSP-Next-{args.model}{q} flow matching {args.frames}f "
                       f"{args.height}x{args.width}", "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "higher_is_better": True, "scaling": "weak" if world > 4 else "strong",
             "dtype": "bf16", "impl": impl,

@@ -7,12 +7,15 @@
 //   (ospnext/modules/osp_next.py:742-777, 873-877, 926-957), text/patch
 //   embeddings and the head (osp_next.py:1092-1104, 1249-1252, want2v.py:262-287).
 //
-// Structure (one CTA per SM, 192 threads):
+// Structure (one CTA per SM, 320 threads):
 //   warp 0      TMA producer: A/B k-blocks into a STAGES-deep smem ring (128B swizzle)
 //   warp 1      MMA issuer:  tcgen05.mma 128×BN×16 per step into one of two TMEM
 //               accumulators (so the epilogue of tile i overlaps the MMAs of tile i+1)
-//   warps 2..5  epilogue:    tcgen05.ld 32 columns at a time, bias / GELU-tanh /
-//               gated fp32 residual (+ row remap = fused layout change), global store
+//   warps 2..9  epilogue:    two groups of four warps (one per TMEM lane quarter), each
+//               taking half of the tile's columns: tcgen05.ld 32 columns at a time, bias /
+//               GELU-tanh / gated fp32 residual (+ row remap = fused layout change), global
+//               store.  Two groups double the global loads in flight, which the residual
+//               epilogue (a streaming fp32 read-modify-write) needs to keep up with the MMAs.
 // Tiles are visited in M-groups of 16 so the weight stays L2-resident across a group.
 // Either operand may instead be MN-major (stored [K, M] / [K, N], MN contiguous): the
 // backward GEMMs dX = dY·W and dW = dYᵀ·X read dY, W and X in place, with no transposed
@@ -30,6 +33,7 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;              // 64 bf16 = 128 B rows (one swizzle span)
 constexpr int kGroupM = 16;
 constexpr int kSmemBudget = 196608;  // 192 KiB of operand ring
+constexpr int kGemmThreads = 320;
 
 enum EpiMode : int { kEpiStore = 0, kEpiResidual = 1 };
 
@@ -66,7 +70,7 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
 }
 
 template <int BN, int MODE, typename OutT, bool A_MN = false, bool B_MN = false>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
   constexpr int STAGES = kSmemBudget / (kBM * kBK * 2 + BN * kBK * 2);
   constexpr uint32_t A_BYTES = kBM * kBK * 2;
@@ -97,7 +101,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], 4); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], 8); }
     mbar_init(done, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -180,8 +184,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       mbar_wait(done, 0, args.err, kErrGemmTeardown);
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    // ---------------------------------------------------------------- epilogue (warps 2..9)
     const int quarter = warp & 3;               // TMEM lanes 32·quarter .. +31
+    const int eg = (warp - 2) >> 2;             // column half of the tile
     int it = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
       if (*abort_flag) break;
@@ -210,7 +215,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       }
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = eg * (BN / 64); c < (eg + 1) * (BN / 64); ++c) {
         const int col0 = nb * BN + c * 32;
         uint32_t r[32];
         tmem_ld32(t_row + c * 32, r);
@@ -263,19 +268,21 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           }
         } else {
           // resid + bf16(y)·gate  (the Linear output is bf16 under autocast in the reference)
+          // the residual stream is read once and written once: streaming (evict-first) accesses
+          // keep it from pushing the L2-resident A/B tiles out
           const float4* r4 = reinterpret_cast<const float4*>(args.resid + (long)row * args.N + col0);
           float4* o4 = reinterpret_cast<float4*>(out_base + out_row * args.N + col0);
           const float4* g4 = args.gate ? reinterpret_cast<const float4*>(args.gate + (long)bidx * args.N + col0)
                                        : nullptr;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            float4 x = r4[j];
+            float4 x = __ldcs(r4 + j);
             float4 g = g4 ? __ldg(g4 + j) : make_float4(1.f, 1.f, 1.f, 1.f);
             x.x += bf16_round(v[4 * j + 0]) * g.x;
             x.y += bf16_round(v[4 * j + 1]) * g.y;
             x.z += bf16_round(v[4 * j + 2]) * g.z;
             x.w += bf16_round(v[4 * j + 3]) * g.w;
-            o4[j] = x;
+            __stcs(o4 + j, x);
           }
         }
       }
@@ -322,7 +329,7 @@ static void launch_gemm(const at::Tensor& a, const at::Tensor& b, GemmArgs& args
   }
   const int tiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
   const int grid = std::max(1, std::min(tiles, num_sms(a.get_device())));
-  kern<<<grid, 192, smem, stream>>>(tmA, tmB, args);
+  kern<<<grid, kGemmThreads, smem, stream>>>(tmA, tmB, args);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

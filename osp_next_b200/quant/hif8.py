@@ -50,8 +50,15 @@ class _HIF8LinearFunction(torch.autograd.Function):
         x2 = x_q.reshape(-1, x_q.shape[-1])
         if g.is_cuda:
             gb = g2.to(torch.bfloat16)
-            dx = ops.linear(gb, w_q.to(torch.bfloat16).t().contiguous(), None, out_dtype=torch.float32)
-            dw = ops.linear(gb.t().contiguous(), x2.to(torch.bfloat16).t().contiguous(), None, out_dtype=torch.float32)
+            wb, xb = w_q.to(torch.bfloat16), x2.to(torch.bfloat16)
+            # operands read MN-major in place; transposed copies only where the shapes miss
+            # the kernel's alignment rules
+            dx = ops.gemm_t(gb, wb, a_mn=False, b_mn=True)
+            if dx is None:
+                dx = ops.linear(gb, wb.t().contiguous(), None, out_dtype=torch.float32)
+            dw = ops.gemm_t(gb, xb, a_mn=True, b_mn=True)
+            if dw is None:
+                dw = ops.linear(gb.t().contiguous(), xb.t().contiguous(), None, out_dtype=torch.float32)
         else:
             dx = g2 @ w_q
             dw = g2.t() @ x2
