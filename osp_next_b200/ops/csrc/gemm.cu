@@ -34,6 +34,8 @@ constexpr int kBK = 64;              // 64 bf16 = 128 B rows (one swizzle span)
 constexpr int kGroupM = 16;
 constexpr int kSmemBudget = 196608;  // 192 KiB of operand ring
 constexpr int kGemmThreads = 320;
+constexpr int kStageRow = 80;                 // bytes per staged row (64 B of bf16 + 16 B pad)
+constexpr int kStageBytes = 32 * kStageRow;   // one epilogue warp's 32 × 32 staging tile
 
 enum EpiMode : int { kEpiStore = 0, kEpiResidual = 1 };
 
@@ -91,6 +93,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   uint64_t* done = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // residual epilogue: per-warp staging of 32 rows × 32 bf16 (row stride 80 B, conflict-free)
+  uint8_t* epi_stage = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(abort_flag + 1) + 127) & ~uintptr_t(127));
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -214,13 +218,33 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         }
       }
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      // residual mode writes rows cooperatively (8 lanes × 16 B = one 128-B row segment):
+      // lane group `sub` handles rows sub, sub+4, …, so gather those rows' destinations once
+      const int sub = lane >> 3, c4 = lane & 7;
+      long t_orow[8];
+      float* t_obase[8];
+      int t_bidx[8];
+      bool t_ok[8];
+      if (MODE == kEpiResidual) {
+        const unsigned long long ob = reinterpret_cast<unsigned long long>(out_base);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int src = i * 4 + sub;
+          t_orow[i] = __shfl_sync(0xffffffffu, out_row, src);
+          t_obase[i] = reinterpret_cast<float*>(__shfl_sync(0xffffffffu, ob, src));
+          t_bidx[i] = __shfl_sync(0xffffffffu, bidx, src);
+          t_ok[i] = __shfl_sync(0xffffffffu, row_ok, src);
+        }
+      }
+      uint8_t* stg = epi_stage + (warp - 2) * kStageBytes;
 #pragma unroll 1
       for (int c = eg * (BN / 64); c < (eg + 1) * (BN / 64); ++c) {
         const int col0 = nb * BN + c * 32;
         uint32_t r[32];
         tmem_ld32(t_row + c * 32, r);
         tmem_ld_wait();
-        if (!row_ok || col0 >= args.N) continue;
+        if (col0 >= args.N) continue;                       // uniform across the warp
+        if (MODE == kEpiStore && !row_ok) continue;
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
@@ -267,23 +291,40 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             for (int j = 0; j < 8; ++j) o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
           }
         } else {
-          // resid + bf16(y)·gate  (the Linear output is bf16 under autocast in the reference)
-          // the residual stream is read once and written once: streaming (evict-first) accesses
-          // keep it from pushing the L2-resident A/B tiles out
-          const float4* r4 = reinterpret_cast<const float4*>(args.resid + (long)row * args.N + col0);
-          float4* o4 = reinterpret_cast<float4*>(out_base + out_row * args.N + col0);
-          const float4* g4 = args.gate ? reinterpret_cast<const float4*>(args.gate + (long)bidx * args.N + col0)
-                                       : nullptr;
+          // resid + bf16(y)·gate (the Linear output is bf16 under autocast in the reference).
+          // bf16(y) goes through smem so that each row is then read, combined and written by
+          // 8 lanes as one contiguous 128-B segment: full-line residual reads and, for the
+          // fused SSP exchange, 128-B writes over NVLink instead of 32 scattered 16-B ones.
+          // The residual stream is touched once: streaming (evict-first) accesses.
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float4 x = __ldcs(r4 + j);
-            float4 g = g4 ? __ldg(g4 + j) : make_float4(1.f, 1.f, 1.f, 1.f);
-            x.x += bf16_round(v[4 * j + 0]) * g.x;
-            x.y += bf16_round(v[4 * j + 1]) * g.y;
-            x.z += bf16_round(v[4 * j + 2]) * g.z;
-            x.w += bf16_round(v[4 * j + 3]) * g.w;
-            __stcs(o4 + j, x);
+          for (int j = 0; j < 4; ++j) {
+            uint4 w;
+            w.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+            w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+            w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+            w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+            *reinterpret_cast<uint4*>(stg + lane * kStageRow + j * 16) = w;
           }
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            if (!t_ok[i]) continue;
+            const int rr = i * 4 + sub;
+            const long grow = (long)mb * kBM + quarter * 32 + rr;
+            const uint2 yy = *reinterpret_cast<const uint2*>(stg + rr * kStageRow + c4 * 8);
+            const float2 y01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&yy.x));
+            const float2 y23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&yy.y));
+            float4 x = __ldcs(reinterpret_cast<const float4*>(args.resid + grow * args.N + col0) + c4);
+            const float4 g = args.gate ? __ldg(reinterpret_cast<const float4*>(args.gate + (long)t_bidx[i] * args.N +
+                                                                               col0) + c4)
+                                       : make_float4(1.f, 1.f, 1.f, 1.f);
+            x.x += y01.x * g.x;
+            x.y += y01.y * g.y;
+            x.z += y23.x * g.z;
+            x.w += y23.y * g.w;
+            __stcs(reinterpret_cast<float4*>(t_obase[i] + t_orow[i] * args.N + col0) + c4, x);
+          }
+          __syncwarp();
         }
       }
       tc_fence_before();
@@ -303,7 +344,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 template <int BN>
 constexpr int gemm_smem_bytes() {
   constexpr int STAGES = kSmemBudget / (kBM * kBK * 2 + BN * kBK * 2);
-  return 1024 + STAGES * (kBM * kBK * 2 + BN * kBK * 2) + (2 * STAGES + 5) * 8 + 16;
+  return 1024 + STAGES * (kBM * kBK * 2 + BN * kBK * 2) + (2 * STAGES + 5) * 8 + 16 + 128 + 8 * kStageBytes;
 }
 
 static int num_sms(int dev) {
