@@ -244,7 +244,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         tmem_ld32(t_row + c * 32, r);
         tmem_ld_wait();
         if (col0 >= args.N) continue;                       // uniform across the warp
-        if (MODE == kEpiStore && !row_ok) continue;
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
@@ -257,7 +256,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           }
         }
         if (MODE == kEpiStore) {
-          if (args.aux) {              // pre-activation kept for the GELU backward
+          if (args.aux && row_ok) {    // pre-activation kept for the GELU backward
             uint4* a4 = reinterpret_cast<uint4*>(args.aux + out_row * args.N + col0);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -273,9 +272,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_f(v[j]);
           }
-          OutT* o = reinterpret_cast<OutT*>(args.out) + out_row * args.N + col0;
+          // bf16: stage the warp's 32 rows × 32 outputs in smem, then write each row's 64 B
+          // as one contiguous segment (4 lanes × 16 B) instead of 32 scattered 16-B stores
           if constexpr (sizeof(OutT) == 2) {
-            uint4* o4 = reinterpret_cast<uint4*>(o);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               uint4 w;
@@ -283,10 +282,22 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
               w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
               w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
               w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
-              o4[j] = w;
+              *reinterpret_cast<uint4*>(stg + lane * kStageRow + j * 16) = w;
             }
-          } else {
-            float4* o4 = reinterpret_cast<float4*>(o);
+            __syncwarp();
+            const int q = lane >> 2, cc = lane & 3;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int rr = i * 8 + q;
+              const long grow = (long)mb * kBM + quarter * 32 + rr;
+              if (grow < args.M)
+                *reinterpret_cast<uint4*>(reinterpret_cast<OutT*>(args.out) + grow * args.N + col0 + cc * 8) =
+                    *reinterpret_cast<const uint4*>(stg + rr * kStageRow + cc * 16);
+            }
+            __syncwarp();
+          } else if (row_ok) {
+            // fp32 (weight gradients): each thread's 128-B row chunk is already a full line
+            float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + out_row * args.N + col0);
 #pragma unroll
             for (int j = 0; j < 8; ++j) o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
           }
