@@ -53,6 +53,12 @@ void p2p_close(int64_t ptr);
 void p2p_free(int64_t ptr);
 at::Tensor p2p_view(int64_t ptr, std::vector<int64_t> shape, at::ScalarType dtype, int64_t device);
 void p2p_barrier(const at::Tensor& flag_ptrs, int64_t rank, int64_t world, int64_t epoch, double limit_s);
+void p2p_barrier_tagged(const at::Tensor& flag_ptrs, int64_t rank, int64_t world, int64_t epoch, int64_t tag,
+                        double limit_s);
+void p2p_gather(const at::Tensor& bases, int64_t off, int64_t shard_bytes, int64_t rank, int64_t world,
+                int64_t abort_ptr);
+void p2p_reduce_scatter_f32(at::Tensor& out, const at::Tensor& bases, int64_t off, int64_t shard_elems, int64_t rank,
+                            int64_t world, double scale, int64_t abort_ptr);
 
 static int* g_err[64] = {nullptr};
 static std::mutex g_err_mu;
@@ -110,5 +116,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_free", &osp::p2p_free);
   m.def("p2p_view", &osp::p2p_view);
   m.def("p2p_barrier", &osp::p2p_barrier);
+  m.def("p2p_barrier_tagged", &osp::p2p_barrier_tagged);
+  m.def("p2p_gather", &osp::p2p_gather);
+  m.def("p2p_reduce_scatter_f32", &osp::p2p_reduce_scatter_f32);
   m.def("get_error", &osp::get_error, pybind11::arg("device"), pybind11::arg("clear") = true);
 }

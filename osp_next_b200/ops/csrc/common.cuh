@@ -20,7 +20,7 @@ enum : int {
   kErrNone = 0,
   kErrGemmProducer = 101, kErrGemmMma = 102, kErrGemmEpilogue = 103, kErrGemmTeardown = 104,
   kErrAttnProducer = 201, kErrAttnMma = 202, kErrAttnSoftmax = 203, kErrAttnTeardown = 204,
-  kErrP2P = 301,
+  kErrP2P = 301, kErrP2PTag = 302,
   kErrProbeMbar = 901, kErrProbeFlag = 902,
 };
 

@@ -14,6 +14,12 @@
 //    %globaltimer — until every peer's slot in its own array reaches `epoch`.
 //    On timeout it records kErrP2P in the error word and returns, so a missing
 //    peer never hangs the GPU; the host checks the error word.
+//  * FSDP collectives over peer memory (parallel/fsdp_comm.py): every rank keeps a ring
+//    of slots in one IPC arena, allocated in the same order on every rank, so a slot has
+//    the same offset everywhere.  A tagged barrier (epoch + the slot's offset, checked
+//    against every peer's) precedes a pull kernel: all-gather copies each peer's shard
+//    out of that peer's slot, reduce-scatter sums this rank's chunk of every peer's slot.
+//    A mismatched offset or a timeout sets an abort word that the pull kernel honours.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -94,6 +100,132 @@ void p2p_barrier(const at::Tensor& flag_ptrs, int64_t rank, int64_t world, int64
   p2p_barrier_kernel<<<1, 32 * ((world + 31) / 32), 0, at::cuda::getCurrentCUDAStream()>>>(
       flag_ptrs.data_ptr<int64_t>(), (int)rank, (int)world, (int)epoch, (unsigned long long)(limit_s * 1e9),
       error_word(flag_ptrs.get_device()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ---------------------------------------------------------------------------- FSDP collectives
+// Flag array layout per rank: [0, world) epochs written by each peer, [world, 3·world) the
+// tag (slot offset) each peer used, one array per epoch parity (a peer can already be one
+// barrier ahead when this rank reads, never two), [3·world] this rank's abort word.
+__global__ void p2p_barrier_tagged_kernel(const int64_t* flag_ptrs, int rank, int world, int epoch, int tag,
+                                          unsigned long long limit_ns, int* err) {
+  const int r = threadIdx.x;
+  int* mine = reinterpret_cast<int*>(flag_ptrs[rank]);
+  const int tag_base = world + (epoch & 1) * world;
+  if (r == 0) mine[3 * world] = 0;
+  if (r < world) {
+    __threadfence_system();
+    int* peer = reinterpret_cast<int*>(flag_ptrs[r]);
+    peer[tag_base + rank] = tag;                   // ordered before the epoch by the release below
+    st_release_sys(peer + rank, epoch);
+  }
+  __syncthreads();
+  if (r < world) {
+    const uint64_t t0 = globaltimer();
+    bool ok = true;
+    while (ld_acquire_sys(mine + r) < epoch) {
+      if (globaltimer() - t0 > limit_ns) {
+        record_error(err, kErrP2P);
+        ok = false;
+        break;
+      }
+      __nanosleep(100);
+    }
+    if (ok && *reinterpret_cast<volatile int*>(mine + tag_base + r) != tag) {
+      record_error(err, kErrP2PTag);
+      ok = false;
+    }
+    if (!ok) atomicExch(mine + 3 * world, 1);
+  }
+}
+
+void p2p_barrier_tagged(const at::Tensor& flag_ptrs, int64_t rank, int64_t world, int64_t epoch, int64_t tag,
+                        double limit_s) {
+  TORCH_CHECK(flag_ptrs.is_cuda() && flag_ptrs.scalar_type() == at::kLong && flag_ptrs.numel() == world &&
+              world <= 1024, "p2p_barrier_tagged: int64 device tensor of peer flag pointers");
+  c10::cuda::CUDAGuard guard(flag_ptrs.device());
+  p2p_barrier_tagged_kernel<<<1, 32 * ((world + 31) / 32), 0, at::cuda::getCurrentCUDAStream()>>>(
+      flag_ptrs.data_ptr<int64_t>(), (int)rank, (int)world, (int)epoch, (int)tag,
+      (unsigned long long)(limit_s * 1e9), error_word(flag_ptrs.get_device()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// All-gather: bases[p] = rank p's arena (peers mapped); copy each peer's shard
+// [off + p·shard, +shard) of its own slot into the same range of this rank's slot.
+template <typename V>
+__global__ void p2p_gather_kernel(const int64_t* bases, long off, long shard_bytes, int rank, int world,
+                                  const int* abort_word) {
+  if (*reinterpret_cast<const volatile int*>(abort_word)) return;
+  const long nv = shard_bytes / (long)sizeof(V);
+  const long total = nv * (world - 1);
+  char* dst = reinterpret_cast<char*>(bases[rank]) + off;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int pi = (int)(i / nv);
+    const int p = pi < rank ? pi : pi + 1;
+    const long j = i - (long)pi * nv;
+    const V* src = reinterpret_cast<const V*>(reinterpret_cast<const char*>(bases[p]) + off + p * shard_bytes) + j;
+    reinterpret_cast<V*>(dst + p * shard_bytes)[j] = *src;
+  }
+}
+
+// Reduce-scatter (fp32): out[i] = scale · Σ_p slot_p[rank·S + i], peers' slots read in place.
+__global__ void p2p_reduce_scatter_f32_kernel(float* __restrict__ out, const int64_t* bases, long off, long S,
+                                              int rank, int world, float scale, const int* abort_word) {
+  if (*reinterpret_cast<const volatile int*>(abort_word)) return;
+  const bool vec = (S % 4) == 0 && (off % 16) == 0;
+  const long n = vec ? S / 4 : S;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    if (vec) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k = 0; k < world; ++k) {
+        const int p = (rank + 1 + k) % world;        // start at a different peer on every rank
+        const float4 v = reinterpret_cast<const float4*>(
+            reinterpret_cast<const char*>(bases[p]) + off + (long)rank * S * 4)[i];
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+      }
+      reinterpret_cast<float4*>(out)[i] = make_float4(acc.x * scale, acc.y * scale, acc.z * scale, acc.w * scale);
+    } else {
+      float acc = 0.f;
+      for (int k = 0; k < world; ++k) {
+        const int p = (rank + 1 + k) % world;
+        acc += reinterpret_cast<const float*>(reinterpret_cast<const char*>(bases[p]) + off + (long)rank * S * 4)[i];
+      }
+      out[i] = acc * scale;
+    }
+  }
+}
+
+static int pull_grid(long work) {
+  return (int)std::max<long>(1, std::min<long>((work + 255) / 256, 148L * 8));
+}
+
+void p2p_gather(const at::Tensor& bases, int64_t off, int64_t shard_bytes, int64_t rank, int64_t world,
+                int64_t abort_ptr) {
+  TORCH_CHECK(bases.is_cuda() && bases.scalar_type() == at::kLong && bases.numel() == world, "p2p_gather: bases");
+  c10::cuda::CUDAGuard guard(bases.device());
+  if (world < 2 || shard_bytes == 0) return;
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int64_t* b = bases.data_ptr<int64_t>();
+  const int* ab = reinterpret_cast<const int*>(abort_ptr);
+  if (shard_bytes % 16 == 0 && off % 16 == 0)
+    p2p_gather_kernel<int4><<<pull_grid(shard_bytes / 16 * (world - 1)), 256, 0, st>>>(b, off, shard_bytes, rank, world, ab);
+  else if (shard_bytes % 4 == 0 && off % 4 == 0)
+    p2p_gather_kernel<int><<<pull_grid(shard_bytes / 4 * (world - 1)), 256, 0, st>>>(b, off, shard_bytes, rank, world, ab);
+  else
+    p2p_gather_kernel<char><<<pull_grid(shard_bytes * (world - 1)), 256, 0, st>>>(b, off, shard_bytes, rank, world, ab);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void p2p_reduce_scatter_f32(at::Tensor& out, const at::Tensor& bases, int64_t off, int64_t shard_elems, int64_t rank,
+                            int64_t world, double scale, int64_t abort_ptr) {
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.is_contiguous() && out.numel() == shard_elems,
+              "p2p_reduce_scatter_f32: fp32 contiguous out [S]");
+  TORCH_CHECK(bases.scalar_type() == at::kLong && bases.numel() == world, "p2p_reduce_scatter_f32: bases");
+  c10::cuda::CUDAGuard guard(out.device());
+  if (shard_elems == 0) return;
+  p2p_reduce_scatter_f32_kernel<<<pull_grid(shard_elems / 4 + 1), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      out.data_ptr<float>(), bases.data_ptr<int64_t>(), off, shard_elems, (int)rank, (int)world, (float)scale,
+      reinterpret_cast<const int*>(abort_ptr));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

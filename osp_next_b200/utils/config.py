@@ -17,7 +17,7 @@ KNOWN_KEYS = {
     "deterministic_training", "profiling", "wandb_config", "model_config", "scheduler_config", "vae_config",
     "text_encoder_config", "data_config", "optimizer_config", "pipeline_name", "prompt_txt", "batch_size",
     "num_frames", "height", "width", "save_fps", "num_epochs", "resume_epoch", "lora_config", "rl_config",
-    "metrics_file", "max_steps", "timeout_s", "legacy_clip_group_sum",
+    "metrics_file", "max_steps", "timeout_s", "legacy_clip_group_sum", "fsdp_p2p_collectives",
 }
 
 

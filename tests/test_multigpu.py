@@ -87,3 +87,58 @@ def test_ssp_matches_single_gpu(ssp, exchange):
             assert o["err"] == 0
             rel = (o["y"] - y1).norm() / y1.norm()
             assert rel < 2e-2, (r, rel)
+
+
+def _fsdp_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    from torch.distributed.device_mesh import init_device_mesh
+    from osp_next_b200.models.osp_next import OSPNextAttentionBlock, OSPNextModel, WanLayerNorm, WanRMSNorm
+    from osp_next_b200.parallel.fsdp import FSDP2_mix_wrapper
+    from osp_next_b200.parallel.fsdp_comm import check, close, enable_p2p_fsdp
+    mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("fsdp",))
+    out = {}
+    for mode in ("nccl", "p2p"):
+        torch.manual_seed(0)
+        with torch.device(dev):
+            m = OSPNextModel(dim=256, ffn_dim=512, num_heads=2, num_layers=4, text_len=16,
+                             skiparse_model_type="dual_end", sparse_ratio=2, num_full_blocks=0)
+            m.head.head.weight.data.normal_(std=0.02)
+        FSDP2_mix_wrapper(m, mesh, torch.bfloat16, main_block_to_half=OSPNextAttentionBlock,
+                          blocks_to_float=[WanLayerNorm, WanRMSNorm])
+        arenas = enable_p2p_fsdp(list(m.blocks), mesh.get_group(), device=dev) if mode == "p2p" else None
+        opt = torch.optim.AdamW(m.parameters(), lr=1e-3)
+        g = torch.Generator().manual_seed(10 + rank)
+        losses = []
+        for _ in range(3):
+            x = torch.randn(1, 16, 3, 16, 16, generator=g).to(dev)
+            ctx = torch.randn(1, 16, 4096, generator=g).to(dev)
+            loss = m(x, torch.tensor([400.0], device=dev), ctx).float().pow(2).mean()
+            loss.backward()
+            opt.step()
+            opt.zero_grad()
+            losses.append(loss.item())
+        if arenas is not None:
+            check(arenas, rank)
+            dist.barrier()
+            close(arenas)
+        out[mode] = (losses, sum(p.to_local().float().sum().item() for p in m.parameters()))
+    torch.save(out, os.path.join(out_dir, f"f{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fsdp_p2p_collectives_match_nccl():
+    """FSDP2 training steps with the NVLink pull all-gather / reduce-scatter give the same
+    losses and parameters as with NCCL collectives."""
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_fsdp_worker, args=(2, _port(), d), nprocs=2, join=True, start_method="spawn")
+        for r in range(2):
+            o = torch.load(os.path.join(d, f"f{r}.pt"))
+            (ln, pn), (lp, pp) = o["nccl"], o["p2p"]
+            for a, b in zip(ln, lp):
+                assert abs(a - b) <= 1e-4 * max(1.0, abs(a)), (ln, lp)
+            assert abs(pn - pp) <= 1e-3 * max(1.0, abs(pn)), (pn, pp)

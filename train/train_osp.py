@@ -87,6 +87,12 @@ def main(config, on_step=None):
         model.set_gradient_checkpointing(True)
     if mesh is not None:
         B.fsdp_wrap(model, config, mesh, weight_dtype)
+    p2p_arenas = None
+    if mesh is not None and dev.type == "cuda" and config.get("fsdp_p2p_collectives", False):
+        # block parameter all-gather / gradient reduce-scatter over NVLink peer memory
+        from osp_next_b200.parallel.fsdp_comm import enable_p2p_fsdp
+        fsdp_dim = mesh["fsdp"] if "ddp" in (mesh.mesh_dim_names or ()) else mesh
+        p2p_arenas = enable_p2p_fsdp(list(model.blocks), fsdp_dim.get_group(), device=dev)
     ema = FSDPEMAModel(model, config.get("ema_decay", 0.9999), config.get("ema_update_interval", 1)) \
         if config.get("ema_decay", 0) else None
     opt = FusedAdamW([p for p in model.parameters() if p.requires_grad], lr=opt_cfg.get("lr", 1e-5),
@@ -193,6 +199,11 @@ def main(config, on_step=None):
                     f.write(json.dumps(rec) + "\n")
         if it % save_interval == 0:
             ckpt.save(it, model, opt, ema, sampler, clipper)
+    if p2p_arenas is not None:
+        from osp_next_b200.parallel.fsdp_comm import check, close
+        check(p2p_arenas, dev.index)
+        dist.barrier()
+        close(p2p_arenas)
     return step_times
 
 
