@@ -206,11 +206,34 @@ def ln_modulate(x, shift, scale, eps):
     return (y * (1 + scale.float()[:, None, :]) + shift.float()[:, None, :]).to(_BF16)
 
 
+class _AffineLNFn(torch.autograd.Function):
+    """bf16 affine LayerNorm of the fp32 residual on the fused kernels: the backward is the
+    LN-modulate backward with (1 + scale) = w for every batch entry (dw = Σ dscale,
+    db = Σ dshift)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps):
+        ctx.save_for_backward(x, weight)
+        ctx.eps = eps
+        ctx.has_b = bias is not None
+        return ops.layer_norm(x, weight, bias, eps)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        scale = (w.float() - 1.0).expand(x.shape[0], -1)
+        dx, dsc, dsh = ops.ln_modulate_bwd(x, dy, scale, ctx.eps)
+        return dx, dsc.sum(0).to(w.dtype), (dsh.sum(0) if ctx.has_b else None), None
+
+
 def layer_norm(x, weight, bias, eps):
     if not x.is_cuda:
         return F.layer_norm(x.float(), (x.shape[-1],), weight, bias, eps).type_as(x)
     if _fused(x, weight, bias):
         return ops.layer_norm(x, weight, bias, eps)
+    if (weight is not None and x.dtype == torch.float32 and x.dim() == 3 and x.shape[-1] % 4 == 0
+            and x.shape[-1] <= 8192):
+        return _AffineLNFn.apply(x.contiguous(), weight, bias, eps)
     w = weight.float() if weight is not None else None
     b = bias.float() if bias is not None else None
     return F.layer_norm(x.float(), (x.shape[-1],), w, b, eps).to(_BF16)

@@ -440,3 +440,21 @@ def test_training_gelu_linear_grads():
     for a, e in zip(got, (x.grad, w.grad, b.grad)):
         assert _rel(a, e) < 2e-2, _rel(a, e)
     _no_device_error()
+
+
+def test_training_affine_layer_norm_grads():
+    from osp_next_b200.models import functional as Fn
+    torch.manual_seed(24)
+    B, n, C = 2, 77, 1024
+    x = torch.randn(B, n, C, device=DEV, requires_grad=True)
+    w = (1 + 0.1 * torch.randn(C, device=DEV)).requires_grad_(True)
+    b = (0.1 * torch.randn(C, device=DEV)).requires_grad_(True)
+    g = torch.randn(B, n, C, device=DEV)
+    (Fn._AffineLNFn.apply(x, w, b, 1e-6).float() * g).sum().backward()
+    got = (x.grad.clone(), w.grad.clone(), b.grad.clone())
+    for t in (x, w, b):
+        t.grad = None
+    (torch.nn.functional.layer_norm(x, (C,), w, b, 1e-6).to(torch.bfloat16).float() * g).sum().backward()
+    for a, e in zip(got, (x.grad, w.grad, b.grad)):
+        assert _rel(a, e) < 1e-2, _rel(a, e)
+    _no_device_error()
