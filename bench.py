@@ -15,6 +15,12 @@ Dense blocks use Ulysses over the SSP ranks.
 ``--impl reference`` runs the unmodified reference (``baseline/_ref``) through its
 own ``FlowMatchingScheduler.sample`` on the same shapes (see baseline/ref_harness.py).
 
+``--mode train`` measures the other BASELINE metric instead: flow-matching training
+tokens/s through ``train/train_osp.py`` (FSDP over all ranks, SSP up to 4, activation
+checkpointing, adaptive clipping, fused AdamW, EMA), synthetic latents and text; the
+reference arm runs the reference's own FSDP2 wrapper, model, scheduler, clipper, EMA and
+``torch.optim.AdamW`` (baseline/ref_train.py).
+
 Timing: W warm-up steps, then K steps between barrier + synchronize on every
 rank; CUDA events on the launching stream; the max over ranks is reported.
 Inputs are 1.6 GB of activations per step (> 126 MB L2), so L2 is not flushed.
