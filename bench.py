@@ -74,7 +74,7 @@ def parse():
     p.add_argument("--quant", choices=["none", "hif8"], default="none",
                    help="train mode: HiF8 fake-quant linears (BASELINE config 4) or plain bf16")
     p.add_argument("--loss-log", default=None, help="train mode: append per-step losses (JSONL) here")
-    p.add_argument("--fsdp-comm", choices=["p2p", "nccl"], default="nccl",
+    p.add_argument("--fsdp-comm", choices=["p2p", "nccl"], default="p2p",
                    help="train mode: FSDP block all-gather / reduce-scatter over NVLink peer memory or NCCL")
     p.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                    help="SSP layout exchange: fused GEMM-epilogue stores over NVLink, or NCCL all_to_all")
@@ -286,7 +286,7 @@ def train_config(args, world, out_dir):
                save_interval=10 ** 9, log_interval=1, fsdp_size=fsdp, skiparse_sp_size=ssp,
                use_skiparse_sequence_parallel=ssp > 1, sp_size=1, use_sequence_parallel=False,
                weight_dtype="bf16", gradient_checkpointing=True, seed=1024,
-               fsdp_p2p_collectives=getattr(args, "fsdp_comm", "nccl") == "p2p")
+               fsdp_p2p_collectives=getattr(args, "fsdp_comm", "p2p") == "p2p")
     cfg["model_config"] = dict(cfg.get("model_config", {}), **{k: v for k, v in PRESETS[args.model].items()})
     cfg["model_config"].pop("pretrained_model_dir_or_checkpoint", None)
     if getattr(args, "quant", "none") == "hif8":
