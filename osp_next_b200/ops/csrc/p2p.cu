@@ -160,8 +160,10 @@ __global__ void p2p_gather_kernel(const int64_t* bases, long off, long shard_byt
   const long total = nv * (world - 1);
   char* dst = reinterpret_cast<char*>(bases[rank]) + off;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    // peers in ring order starting after this rank, so that at any moment every rank is
+    // pulling from a different peer instead of all of them hammering rank 0's links
     const int pi = (int)(i / nv);
-    const int p = pi < rank ? pi : pi + 1;
+    const int p = (rank + 1 + pi) % world;
     const long j = i - (long)pi * nv;
     const V* src = reinterpret_cast<const V*>(reinterpret_cast<const char*>(bases[p]) + off + p * shard_bytes) + j;
     reinterpret_cast<V*>(dst + p * shard_bytes)[j] = *src;
