@@ -146,7 +146,11 @@ def main(config):
         return t5([prompts[pid]]).to(wdt)
 
     epochs = config.get("num_epochs", 1000)
+    import time as _time
     for epoch in range(start_epoch, epochs):
+        if dev.type == "cuda":
+            torch.cuda.synchronize()
+        t_epoch = _time.perf_counter()
         # ------------------------------------------------ rollout
         gen = torch.Generator().manual_seed(seed + epoch)
         m = max(1, (dp * sbs * rl.get("num_batches_per_epoch", 1)) // k)
@@ -185,6 +189,9 @@ def main(config):
             adv_all = (all_r - all_r.mean()) / (all_r.std() + 1e-4)
         n_local = len(local_r)
         adv_local = torch.tensor(adv_all[dp_rank * n_local:(dp_rank + 1) * n_local], dtype=torch.float32)
+        if dev.type == "cuda":
+            torch.cuda.synchronize()
+        t_rollout = _time.perf_counter() - t_epoch
         # ------------------------------------------------ policy update
         policy.train()
         off = 0
@@ -207,8 +214,13 @@ def main(config):
             global_step += 1
             if ema is not None:
                 ema.update(policy, global_step)
+        if dev.type == "cuda":
+            torch.cuda.synchronize()
+        t_total = _time.perf_counter() - t_epoch
         log_on_main_process(logger, json.dumps({
-            "epoch": epoch, "global_step": global_step, "reward_mean": float(np.mean(all_r)),
+            "epoch": epoch, "global_step": global_step, "rollout_s": round(t_rollout, 3),
+            "train_s": round(t_total - t_rollout, 3), "epoch_s": round(t_total, 3),
+            "reward_mean": float(np.mean(all_r)),
             "reward_std": float(np.std(all_r)), **{k_: float(v) for k_, v in info.items()}}))
         if (epoch + 1) % config.get("save_interval", 100) == 0 or epoch + 1 == epochs:
             path = save_lora(policy, out_dir, global_step)
