@@ -43,7 +43,7 @@ import torch.distributed as dist
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-BASELINE_SEC_PER_VIDEO = None   # the reference publishes only speed-up ratios
+BASELINE_SEC_PER_VIDEO = None   # the reference publishes only speed-up ratios, no absolute sec/video
 STEPS_PER_VIDEO = 50
 
 PRESETS = {
@@ -347,8 +347,8 @@ def run_train(args, rank, world, local, impl):
             "warmup": args.warmup, "higher_is_better": True, "scaling": "weak" if world > 4 else "strong",
             "dtype": "bf16", "impl": impl,
             "data": "synthetic (random-init weights, N(0,1) latents and text embeddings, logit-normal t)",
+            "layout": {"fsdp_comm": args.fsdp_comm if impl == "ours" else "nccl"},
             "config": {"model": f"OSP-Next-{args.model}", "global_batch": max(1, world // ssp),
-                       "fsdp_comm": args.fsdp_comm if impl == "ours" else "nccl",
                        "seq_len": tokens(args), "parallelism": f"fsdp{fsdp}_ssp{ssp}_dp{max(1, world // ssp)}",
                        "activation_checkpointing": True, "optimizer": "AdamW + adaptive clip + EMA",
                        "l2": "no flush: per-step activations exceed the 126 MB L2"},
@@ -407,7 +407,40 @@ def run_reference(args, rank, world, local):
         clocks = clock.stop()
     ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
     clocks["attention_backend"] = "flash_attn2" if fa2 else "sdpa"
-    return (ms, clocks), None
+    e2e = None
+    if not args.no_e2e:
+        e2e = reference_e2e(args, model, sched, text, neg, lat)
+    return (ms, clocks, e2e), None
+
+
+def reference_e2e(args, model, sched, text, neg, lat):
+    """End to end through the reference's own code: its T2VInferencePipeline.prepare_latents
+    (device copy + SP broadcast) and FlowMatchingScheduler.sample, with prompt embeddings and
+    the initial latent copied from pinned host memory inside the timed region and the final
+    latent read back.  The pipeline's ``__call__`` always VAE-decodes and draws its own noise,
+    so its two denoising building blocks are called directly on the same inputs as ours."""
+    sys.path.insert(0, os.path.join(ROOT, "baseline"))
+    from ospnext.pipelines.t2v_pipeline import T2VInferencePipeline as RefPipeline
+    pipe = RefPipeline(vae=None, tokenizer=None, text_encoder=None, predictor=model, scheduler=sched)
+    text_h, neg_h, lat_h = text.cpu().pin_memory(), neg.cpu().pin_memory(), lat.cpu().pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in (text_h, neg_h, lat_h))
+    dev = lat.device
+    sched.num_inference_steps = args.steps
+    with torch.no_grad():
+        barrier_sync()
+        t0 = time.perf_counter()
+        pe = text_h.to(dev, non_blocking=True)
+        ne = neg_h.to(dev, non_blocking=True)
+        latents = pipe.prepare_latents(lat_h.shape, generator=None, device=dev, dtype=pe.dtype, latents=lat_h)
+        out = sched.sample(model=model, latents=latents, prompt_embeds=pe, negative_prompt_embeds=ne)
+        out_h = out.to("cpu")
+        barrier_sync()
+        e2e_s = max_over_ranks(time.perf_counter() - t0)
+    d2h = out_h.numel() * out_h.element_size()
+    return {"value": round(e2e_s / args.steps * STEPS_PER_VIDEO, 3), "unit": "s/video",
+            "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": d2h // args.steps,
+            "note": "reference T2VInferencePipeline.prepare_latents + FlowMatchingScheduler.sample; "
+                    "inputs from pinned host, latent read back"}
 
 
 # ----------------------------------------------------------------------------- main
@@ -437,9 +470,10 @@ def main():
             "unit": "s/video", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": False, "scaling": "strong", "dtype": "bf16",
             "data": "synthetic (random-init 14B weights, N(0,1) latents and 512x4096 text embeddings)",
+            # the workload only (identical for both arms); the parallel layout is reported in "layout"
             "config": {"model": f"OSP-Next-{args.model}", "global_batch": 1, "seq_len": tokens(args),
                        "latent": list(latent_shape(args)), "steps_per_video": STEPS_PER_VIDEO,
-                       "guidance_scale": args.guidance, "parallelism": par,
+                       "guidance_scale": args.guidance, "parallelism": f"{world}gpu_sequence_parallel",
                        "l2": "no flush: per-step activations (1.6 GB) exceed the 126 MB L2"}}
     if args.impl == "reference":
         res, why = run_reference(args, rank, world, local)
@@ -447,10 +481,10 @@ def main():
             if res is None:
                 print(json.dumps({"impl": "reference", "unavailable": why}))
             else:
-                ms, clocks = res
+                ms, clocks, e2e = res
                 line = dict(base, impl="reference", value=round(ms * STEPS_PER_VIDEO / 1000, 3),
-                            ms_per_step=round(ms, 2), vs_baseline=None, clocks=clocks)
-                line["config"] = dict(base["config"], parallelism=f"ssp{min(world, 4)}_ulysses{max(1, world // 4)}")
+                            ms_per_step=round(ms, 2), vs_baseline=None, clocks=clocks, e2e=e2e,
+                            layout=f"ssp{min(world, 4)}_ulysses{max(1, world // 4)}")
                 print(json.dumps(line))
     else:
         ms, launches, clocks, e2e, extra = run_ours(args, rank, world, local)
@@ -458,7 +492,7 @@ def main():
             val = ms * STEPS_PER_VIDEO / 1000.0
             line = dict(base, impl="ours", value=round(val, 3), ms_per_step=round(ms, 2),
                         vs_baseline=(None if BASELINE_SEC_PER_VIDEO is None else BASELINE_SEC_PER_VIDEO / val),
-                        gpu_launches=launches, clocks=clocks, e2e=e2e, checks=extra)
+                        gpu_launches=launches, clocks=clocks, e2e=e2e, checks=extra, layout=par)
             print(json.dumps(line))
     if dist.is_initialized():
         dist.barrier()

@@ -1,6 +1,6 @@
 """Exposed communication time of a training step (analysis tool, not a bench number).
 
-``torchrun --nproc-per-node N -m osp_next_b200.parallel.bench_exposed_comm [bench.py train flags]``
+``torchrun --nproc-per-node N -m benchmarks.exposed_comm [bench.py train flags]``
 runs the same trainer as ``bench.py --mode train`` and records, on every rank, the device
 kernels of the last two steps with the PyTorch profiler.  Per step:
 
@@ -22,7 +22,7 @@ import tempfile
 import torch
 import torch.distributed as dist
 
-ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 COMM_MARKERS = ("nccl", "p2p_barrier", "p2p_gather", "p2p_reduce_scatter")
 
 

@@ -1,6 +1,6 @@
 """Bandwidth of the NVLink pull all-gather / reduce-scatter used for FSDP, against NCCL.
 
-``torchrun --nproc-per-node N -m osp_next_b200.parallel.bench_fsdp_comm``: one 14B block's
+``torchrun --nproc-per-node N -m benchmarks.fsdp_comm``: one 14B block's
 worth of data (351 M parameters: 702 MB bf16 gathered, 1.40 GB fp32 reduce-scattered),
 CUDA events on every rank, min of 5 after warm-up, max over ranks.  Roofline = bytes each
 rank pulls over NVLink ((N−1)/N of the buffer) ÷ 770 GB/s per direction.
@@ -13,8 +13,8 @@ import os
 import torch
 import torch.distributed as dist
 
-from .. import ops
-from .fsdp_comm import _Arena
+from osp_next_b200 import ops
+from osp_next_b200.parallel.fsdp_comm import _Arena
 
 NVLINK_GBS = 770.0
 BLOCK_PARAMS = 351_000_000

@@ -1,6 +1,6 @@
 """Per-kernel benchmarks at the 14B production shapes (and small cases for profiling).
 
-``python -m osp_next_b200.ops.bench_kernels [--case NAME ...] [--size full|small] [--iters N]``
+``python -m benchmarks.kernels [--case NAME ...] [--size full|small] [--iters N]``
 
 Each case is timed with CUDA events on the launching stream after warm-up
 (median of ``iters``); inputs exceed the 126 MB L2 at ``--size full``.  Output:
@@ -17,10 +17,10 @@ import statistics
 
 import torch
 
-from . import attention, attention_bwd, gemm_t, linear, linear_gated_residual, ln_modulate, qk_norm_rope
-from .reference import rope_freqs
+from osp_next_b200.ops import attention, attention_bwd, gemm_t, linear, linear_gated_residual, ln_modulate, qk_norm_rope
+from osp_next_b200.ops.reference import rope_freqs
 
-ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def peaks():

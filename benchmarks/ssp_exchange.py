@@ -1,6 +1,6 @@
 """Roofline benchmark of the fused SSP exchange (FFN-down GEMM + P2P row stores).
 
-Run one process per GPU (``torchrun --nproc-per-node N -m osp_next_b200.parallel.bench_exchange``).
+Run one process per GPU (``torchrun --nproc-per-node N -m benchmarks.ssp_exchange``).
 At the 14B shapes (81f 768×1280 → grid 21×48×80, P = 2) each rank holds its Token-layout
 rows; the FFN-down + gated-residual GEMM of that block writes every output row straight
 into the rank that owns it in the next (Group) layout.  Timed, on every rank with CUDA
@@ -22,15 +22,15 @@ import os
 import torch
 import torch.distributed as dist
 
-from .. import ops
-from ..models.layout import GROUP, TOKEN, ParallelSpec, make_layout, make_redistribution
-from .p2p import P2PExchange
+from osp_next_b200 import ops
+from osp_next_b200.models.layout import GROUP, TOKEN, ParallelSpec, make_layout, make_redistribution
+from osp_next_b200.parallel.p2p import P2PExchange
 
 NVLINK_GBS = 770.0
 
 
 def _peak_tflops() -> float:
-    p = os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")
+    p = os.path.join(os.path.dirname(__file__), "..", "MEASURED_PEAKS.json")
     try:
         with open(p) as f:
             d = json.load(f)

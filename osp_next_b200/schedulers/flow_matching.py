@@ -10,37 +10,63 @@ when the predictor accepts it (``batch_cfg=True``).
 """
 from __future__ import annotations
 
-import logging
 import math
-from typing import Callable, Optional
+from dataclasses import dataclass
+from typing import Callable, Optional, Tuple
 
 import torch
 
 from .. import ops
 
 
+@dataclass(frozen=True)
+class ShiftRule:
+    """Time shift of the flow-matching schedule: σ ↦ s·σ / (1 + (s − 1)·σ).
+
+    ``s`` is either a constant or resolution dependent, ``s = exp(slope·L + intercept)``
+    with ``L`` the latent tokens per frame, the line passing through
+    (``base_image_seq``, ``base_shift``) and (``max_image_seq``, ``max_shift``) in log space.
+    """
+    constant: float = 1.0
+    log_line: Optional[Tuple[float, float]] = None      # (slope, intercept) of log s against L
+
+    @classmethod
+    def through(cls, seq_lo: float, log_s_lo: float, seq_hi: float, log_s_hi: float) -> "ShiftRule":
+        slope = (log_s_hi - log_s_lo) / (seq_hi - seq_lo)
+        return cls(log_line=(slope, log_s_lo - slope * seq_lo))
+
+    def factor(self, seq_len: Optional[int]) -> float:
+        if self.log_line is None:
+            return self.constant
+        if seq_len is None:
+            raise ValueError("a resolution-dependent shift needs image_seq_len (latent tokens per frame)")
+        slope, intercept = self.log_line
+        return math.exp(slope * seq_len + intercept)
+
+    def __call__(self, sigmas: torch.Tensor, seq_len: Optional[int] = None) -> torch.Tensor:
+        s = self.factor(seq_len)
+        return s * sigmas / (1 + (s - 1) * sigmas)
+
+
 class FlowMatchingScheduler:
+    """Keyword names follow the reference's YAML configs (``shift``, ``use_dynamic_shifting``
+    with ``base_image_seq`` / ``max_image_seq`` / ``base_shift`` / ``max_shift``,
+    ``use_logitnorm_time_sampling`` with ``logit_mean`` / ``logit_std``)."""
+
     def __init__(self, num_inference_steps=None, guidance_scale=0.0, use_dynamic_shifting=False,
-                 use_logitnorm_time_sampling=False, shift=1.0, **kwargs):
+                 use_logitnorm_time_sampling=False, shift=1.0, batch_cfg=True, base_image_seq=256,
+                 max_image_seq=4096, base_shift=0.5, max_shift=1.15, logit_mean=0.0, logit_std=1.0, **unused):
         self.num_inference_steps = num_inference_steps
         self.guidance_scale = guidance_scale
         self.do_classifier_free_guidance = guidance_scale > 1.0
-        self.use_dynamic_shifting = use_dynamic_shifting
         self.shift = shift
+        self.use_dynamic_shifting = use_dynamic_shifting
         self.use_logitnorm_time_sampling = use_logitnorm_time_sampling
-        if use_dynamic_shifting:
-            self.base_image_seq = kwargs.pop("base_image_seq", 256)
-            self.max_image_seq = kwargs.pop("max_image_seq", 4096)
-            self.base_shift = kwargs.pop("base_shift", 0.5)
-            self.max_shift = kwargs.pop("max_shift", 1.15)
-            self.shift_k = (self.max_shift - self.base_shift) / (self.max_image_seq - self.base_image_seq)
-            self.shift_b = self.base_shift - self.shift_k * self.base_image_seq
-        if use_logitnorm_time_sampling:
-            self.logit_mean = kwargs.pop("logit_mean", 0.0)
-            self.logit_std = kwargs.pop("logit_std", 1.0)
-        self._sigma_min = 0.0
-        self._sigma_max = 1.0
-        self.batch_cfg = kwargs.pop("batch_cfg", True)
+        self.shift_rule = (ShiftRule.through(base_image_seq, base_shift, max_image_seq, max_shift)
+                           if use_dynamic_shifting else ShiftRule(constant=shift))
+        self.logit_normal = (logit_mean, logit_std) if use_logitnorm_time_sampling else None
+        self.batch_cfg = batch_cfg
+        self._sigma_min, self._sigma_max = 0.0, 1.0
 
     @property
     def sigma_min(self):
@@ -49,6 +75,26 @@ class FlowMatchingScheduler:
     @property
     def sigma_max(self):
         return self._sigma_max
+
+    def draw_training_sigmas(self, batch_size, device=torch.device("cpu")):
+        """Unshifted σ per sample: U[0, 1), or sigmoid of N(mean, std) (logit-normal)."""
+        if self.logit_normal is None:
+            return torch.rand((batch_size,), device=device)
+        mean, std = self.logit_normal
+        return torch.sigmoid(torch.randn((batch_size,), device=device) * std + mean)
+
+    def inference_grid(self, device=torch.device("cpu")):
+        """Unshifted σ of the sampler: num_inference_steps + 1 points from σ_max down to σ_min."""
+        return torch.linspace(self._sigma_max, self._sigma_min, self.num_inference_steps + 1, device=device)
+
+    def _set_sigmas(self, sigmas=None, batch_size=None, image_seq_len=None, training=True,
+                    device=torch.device("cpu")):
+        """Shifted σ: the sampler grid (``training=False``), else the given or freshly drawn σ."""
+        if not training:
+            base = self.inference_grid(device)
+        else:
+            base = self.draw_training_sigmas(batch_size, device) if sigmas is None else sigmas
+        return self.shift_rule(base, image_seq_len)
 
     # ------------------------------------------------------------------ training
     def interpolation(self, latents, prior_dist, sigmas):
@@ -75,25 +121,6 @@ class FlowMatchingScheduler:
         x_t = self.interpolation(latents, prior_dist, sigmas)
         return dict(x_t=x_t, prior_dist=prior_dist, sigmas=sigmas, timesteps=timesteps)
 
-    def _set_sigmas(self, sigmas=None, batch_size=None, image_seq_len=None, training=True,
-                    device=torch.device("cpu")):
-        if training:
-            if sigmas is None:
-                if self.use_logitnorm_time_sampling:
-                    sigmas = torch.sigmoid(torch.normal(mean=self.logit_mean, std=self.logit_std,
-                                                        size=(batch_size,), device=device))
-                else:
-                    sigmas = torch.rand((batch_size,), device=device)
-        else:
-            sigmas = torch.linspace(self.sigma_max, self.sigma_min, self.num_inference_steps + 1, device=device)
-        if self.use_dynamic_shifting:
-            if image_seq_len is None:
-                raise ValueError("you have to pass `image_seq_len` when `use_dynamic_shifting` is set to be `True`")
-            shift = math.exp(image_seq_len * self.shift_k + self.shift_b)
-        else:
-            shift = self.shift
-        return shift * sigmas / (1 + (shift - 1) * sigmas)
-
     def _training_weight(self, sigmas):
         return 1.0
 
@@ -110,7 +137,7 @@ class FlowMatchingScheduler:
 
     def sample(self, model, latents, prompt_embeds=None, negative_prompt_embeds=None,
                step_callback: Optional[Callable] = None, cfg_parallel=None, max_steps=None,
-               cuda_graph: bool = False, **model_kwargs):
+               cuda_graph: bool = False, check_errors_every: int = 1, **model_kwargs):
         """Euler sampling with CFG.
 
         ``cfg_parallel``: optional :class:`osp_next_b200.parallel.cfg.CFGParallel`
@@ -118,6 +145,9 @@ class FlowMatchingScheduler:
         ``max_steps``: stop after the first steps of the schedule (timing runs).
         ``cuda_graph``: capture the model call once (after one eager warm-up step) and
         replay it for the remaining steps; single-GPU CUDA inference only.
+        ``check_errors_every``: every that many steps (and after the last) read the device
+        error word and raise :class:`osp_next_b200.ops.DeviceWaitError` if a bounded wait in
+        a kernel gave up (e.g. a peer stalled in the NVLink exchange); 0 disables.
         """
         n = self.num_inference_steps
         sigmas = self._set_sigmas(training=False)
@@ -134,7 +164,8 @@ class FlowMatchingScheduler:
         e2 = None
         if cfg and cfg_parallel is None and self.batch_cfg:
             e2 = torch.cat([prompt_embeds, negative_prompt_embeds], 0)
-        for i in range(n if max_steps is None else min(n, max_steps)):
+        n_run = n if max_steps is None else min(n, max_steps)
+        for i in range(n_run):
             t = timesteps[i]
             dt_sigma = float(sigmas[i + 1] - sigmas[i])
             B = latents.shape[0]
@@ -158,6 +189,8 @@ class FlowMatchingScheduler:
                 latents = self._step(pred, latents, dt_sigma)
             if step_callback is not None:
                 step_callback(i, latents)
+            if check_errors_every and latents.is_cuda and ((i + 1) % check_errors_every == 0 or i + 1 == n_run):
+                ops.check_device_errors(latents.device, where=f"sampling step {i}")
         return latents
 
 
