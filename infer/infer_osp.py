@@ -21,6 +21,7 @@ import torch.distributed as dist
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
+from osp_next_b200 import ops  # noqa: E402
 from osp_next_b200.engine import builders as B  # noqa: E402
 from osp_next_b200.parallel.cfg import CFGParallel  # noqa: E402
 from osp_next_b200.parallel.dist_utils import gather_tensor_list_to_one, setup_distributed_env  # noqa: E402
@@ -75,6 +76,7 @@ def main(config):
         vid = pipe(batch, num_frames=config.get("num_frames", 49), height=config.get("height", 480),
                    width=config.get("width", 832), seed=config.get("seed", 42) + i, device=dev,
                    cfg_parallel=cfg_par)
+        ops.check_device_errors(dev, where=f"prompt {i}")    # VAE decode / final step of this video
         if rank % gsp == 0:
             for j, v in enumerate(vid):
                 save_video(v, os.path.join(out_dir, f"{i + j:05d}.mp4"), fps=config.get("save_fps", 16))

@@ -29,6 +29,7 @@ import torch
 import torch.nn as nn
 import torch.utils.checkpoint
 
+from ..utils.profiling import nvtx_range
 from . import functional as Fn
 from .layout import (FULL, GROUP, TOKEN, ParallelSpec, TokenLayout, block_schedule,
                      make_layout, make_redistribution, token_positions)
@@ -137,6 +138,13 @@ class OSPNextSelfAttention(nn.Module):
             return Fn.qkv_norm_rope(x, (self.q.weight, self.k.weight, self.v.weight),
                                     (self.q.bias, self.k.bias, self.v.bias), self.norm_q(None, weight_only=True),
                                     self.norm_k(None, weight_only=True), ctx.pos, ctx.freqs, H, self.eps)
+        if x.is_cuda and self.qk_norm and ctx.pos is not None and (D * H) % 4 == 0:
+            # wrapped projections (LoRA, HiF8) run their own forward; the q/k RMSNorm and the
+            # RoPE stay on the fused kernel (forward and backward) whatever the Linear type
+            qkv = torch.cat([_lin(self.q, x), _lin(self.k, x), _lin(self.v, x)], dim=-1)
+            wq = self.norm_q(None, weight_only=True) if torch.is_grad_enabled() else self.norm_q.weight
+            wk = self.norm_k(None, weight_only=True) if torch.is_grad_enabled() else self.norm_k.weight
+            return Fn.qk_norm_rope_packed(qkv, wq, wk, ctx.pos, ctx.freqs, H, self.eps)
         q = self.norm_q(_lin(self.q, x)).view(B, n, H, D)
         k = self.norm_k(_lin(self.k, x)).view(B, n, H, D)
         v = _lin(self.v, x).view(B, n, H, D)
@@ -493,7 +501,8 @@ class OSPNextModel(nn.Module):
                 if kv is None:
                     kv = block.cross_attn.text_kv(text)
                     self._text_kv_cache[key] = kv
-            x = block(x, e0, text, ctx, kv, gradient_checkpointing=self.gradient_checkpointing)
+            with nvtx_range(f"block{i}_{kind}"):
+                x = block(x, e0, text, ctx, kv, gradient_checkpointing=self.gradient_checkpointing)
             if ctx.relaid:                   # the FFN-down epilogue already stored the next layout
                 if ctx.p2p is not None:      # peers wrote into our buffer: order, then read it
                     p2p.barrier()

@@ -196,6 +196,17 @@ def gated_add_bwd(dout, y, gate):
     return dy, part.sum(1)
 
 
+def rms_norm_bwd(x, dy, weight, eps: float = 1e-6):
+    """Gradient of :func:`rms_norm` → (dx bf16 like x, dweight fp32 [C])."""
+    C = x.shape[-1]
+    x2 = x.reshape(-1, C).to(_BF16).contiguous()
+    dy2 = dy.reshape(-1, C).to(_BF16).contiguous()
+    dx = torch.empty_like(x2)
+    part = torch.empty(_chunks(x2.shape[0]), C, dtype=torch.float32, device=x.device)
+    ext().rms_norm_bwd(x2, dy2, weight.float().contiguous() if weight is not None else None, dx, part, float(eps))
+    return dx.view(x.shape), part.sum(0)
+
+
 def qk_norm_rope_bwd(raw, dq, dk, dv, wq, wk, pos, freqs, eps: float = 1e-6):
     """Gradient of :func:`qk_norm_rope` w.r.t. the fused qkv [B,n,3C] and the two norm
     weights; ``raw`` = the pre-norm q|k [B,n,2C] (bf16), dq/dk/dv [B,n,H,D]."""
@@ -364,3 +375,64 @@ def hif8_quant_dequant(x, scale_max: float = 15.0):
     out = torch.empty_like(xc)
     ext().hif8_qdq(xc, out, float(scale_max))
     return out
+
+
+# ----------------------------------------------------------------------------- device errors
+
+ERROR_NAMES = {
+    101: "GEMM producer wait", 102: "GEMM MMA wait", 103: "GEMM epilogue wait", 104: "GEMM teardown",
+    201: "attention producer wait", 202: "attention MMA wait", 203: "attention softmax wait",
+    204: "attention teardown", 205: "attention shared-memory alignment",
+    301: "NVLink peer barrier timeout", 302: "NVLink peer barrier slot mismatch",
+    901: "probe mbarrier wait", 902: "probe flag wait",
+}
+
+
+class DeviceWaitError(RuntimeError):
+    """A bounded wait inside one of the framework's kernels gave up (a peer rank stalled or
+    died, or a pipeline stage never arrived).  The kernel skipped its remaining work, so
+    the results of the step that raised are not valid."""
+
+    def __init__(self, code: int, device: int, where: str = ""):
+        self.code = code
+        self.device = device
+        name = ERROR_NAMES.get(code, "unknown")
+        super().__init__(f"device {device}: kernel error {code} ({name})" + (f" during {where}" if where else ""))
+
+
+def check_device_errors(device=None, where: str = "") -> None:
+    """Read (and clear) the device error word; raise :class:`DeviceWaitError` if it is set.
+
+    One 4-byte device read after a device synchronize: call it at step boundaries (the
+    samplers and trainers do) and before writing a checkpoint.  No-op without a GPU."""
+    if not torch.cuda.is_available():
+        return
+    if device is None:
+        device = torch.cuda.current_device()
+    elif isinstance(device, torch.device):
+        if device.type != "cuda":
+            return
+        device = device.index if device.index is not None else torch.cuda.current_device()
+    code = int(ext().get_error(int(device), True))
+    if code:
+        raise DeviceWaitError(code, int(device), where)
+
+
+def check_device_errors_all_ranks(device, where: str = "", group=None) -> None:
+    """:func:`check_device_errors` agreed over the process group: every rank raises if any
+    rank's kernels recorded an error, so all ranks stop at the same step boundary."""
+    import torch.distributed as dist
+    code = 0
+    dev_index = None
+    if torch.cuda.is_available() and (not isinstance(device, torch.device) or device.type == "cuda"):
+        dev_index = device.index if isinstance(device, torch.device) else int(device)
+        if dev_index is None:
+            dev_index = torch.cuda.current_device()
+        code = int(ext().get_error(dev_index, True))
+    if dist.is_available() and dist.is_initialized():
+        t = torch.tensor([code], dtype=torch.int64,
+                         device=torch.device("cuda", dev_index) if dev_index is not None else "cpu")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        code = int(t.item())
+    if code:
+        raise DeviceWaitError(code, -1 if dev_index is None else dev_index, (where + " (some rank)").strip())

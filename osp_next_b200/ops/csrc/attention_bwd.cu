@@ -585,11 +585,8 @@ attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 
 // ---------------------------------------------------------------------------- host
 template <typename K>
-static void set_smem(K kernel, int bytes, bool& done) {
-  if (!done) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-    done = true;
-  }
+static void set_smem(K kernel, int bytes) {
+  smem_opt_in(reinterpret_cast<const void*>(kernel), bytes);
 }
 
 void attention_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
@@ -645,12 +642,10 @@ void attention_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   if (max_k > 0) {
     dim3 grid((unsigned)((max_k + bwd::kT - 1) / bwd::kT), (unsigned)nseg, (unsigned)(B * H));
     if (D == 128) {
-      static bool cfg = false;
-      set_smem(attn_bwd_dkdv_kernel<128>, DkdvSmem<128>::BYTES, cfg);
+      set_smem(attn_bwd_dkdv_kernel<128>, DkdvSmem<128>::BYTES);
       attn_bwd_dkdv_kernel<128><<<grid, bwd::kThreads, DkdvSmem<128>::BYTES, stream>>>(tq, tk, tv, tdo, a);
     } else {
-      static bool cfg = false;
-      set_smem(attn_bwd_dkdv_kernel<64>, DkdvSmem<64>::BYTES, cfg);
+      set_smem(attn_bwd_dkdv_kernel<64>, DkdvSmem<64>::BYTES);
       attn_bwd_dkdv_kernel<64><<<grid, bwd::kThreads, DkdvSmem<64>::BYTES, stream>>>(tq, tk, tv, tdo, a);
     }
     C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -658,12 +653,10 @@ void attention_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   if (max_q > 0) {
     dim3 grid((unsigned)((max_q + bwd::kT - 1) / bwd::kT), (unsigned)nseg, (unsigned)(B * H));
     if (D == 128) {
-      static bool cfg = false;
-      set_smem(attn_bwd_dq_kernel<128>, DqSmem<128>::BYTES, cfg);
+      set_smem(attn_bwd_dq_kernel<128>, DqSmem<128>::BYTES);
       attn_bwd_dq_kernel<128><<<grid, bwd::kThreads, DqSmem<128>::BYTES, stream>>>(tq, tk, tv, tdo, a);
     } else {
-      static bool cfg = false;
-      set_smem(attn_bwd_dq_kernel<64>, DqSmem<64>::BYTES, cfg);
+      set_smem(attn_bwd_dq_kernel<64>, DqSmem<64>::BYTES);
       attn_bwd_dq_kernel<64><<<grid, bwd::kThreads, DqSmem<64>::BYTES, stream>>>(tq, tk, tv, tdo, a);
     }
     C10_CUDA_KERNEL_LAUNCH_CHECK();

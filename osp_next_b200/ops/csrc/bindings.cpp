@@ -2,7 +2,9 @@
 #include <torch/extension.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cuda_runtime.h>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "tma_host.h"
 
@@ -23,6 +25,8 @@ void qk_norm_rope_bwd(const at::Tensor& raw, const at::Tensor& g, const at::Tens
                       const at::Tensor& freqs, at::Tensor& dqkv, at::Tensor& dw_part, int64_t part, int64_t B,
                       int64_t n, int64_t C, int64_t D, double eps);
 void gelu_tanh_bwd(const at::Tensor& dh, const at::Tensor& pre, at::Tensor& dpre);
+void rms_norm_bwd(const at::Tensor& x, const at::Tensor& dy, const c10::optional<at::Tensor>& w, at::Tensor& dx,
+                  at::Tensor& dw_part, double eps);
 void ln_modulate(const at::Tensor& x, const c10::optional<at::Tensor>& shift, const c10::optional<at::Tensor>& scale,
                  const c10::optional<at::Tensor>& w, const c10::optional<at::Tensor>& b, at::Tensor& out, double eps);
 void rms_norm(const at::Tensor& x, const c10::optional<at::Tensor>& w, at::Tensor& out, double eps);
@@ -60,10 +64,15 @@ void p2p_gather(const at::Tensor& bases, int64_t off, int64_t shard_bytes, int64
 void p2p_reduce_scatter_f32(at::Tensor& out, const at::Tensor& bases, int64_t off, int64_t shard_elems, int64_t rank,
                             int64_t world, double scale, int64_t abort_ptr);
 
-static int* g_err[64] = {nullptr};
+static int* g_err[kMaxDevices] = {nullptr};
 static std::mutex g_err_mu;
 
+static void check_device(int device) {
+  TORCH_CHECK(device >= 0 && device < kMaxDevices, "device ordinal ", device, " out of range [0, ", kMaxDevices, ")");
+}
+
 int* error_word(int device) {
+  check_device(device);
   std::lock_guard<std::mutex> lk(g_err_mu);
   if (!g_err[device]) {
     c10::cuda::CUDAGuard guard(device);
@@ -71,6 +80,28 @@ int* error_word(int device) {
     C10_CUDA_CHECK(cudaMemset(g_err[device], 0, sizeof(int)));
   }
   return g_err[device];
+}
+
+int num_sms(int device) {
+  check_device(device);
+  static int cache[kMaxDevices] = {0};
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!cache[device]) C10_CUDA_CHECK(cudaDeviceGetAttribute(&cache[device], cudaDevAttrMultiProcessorCount, device));
+  return cache[device];
+}
+
+void smem_opt_in(const void* kernel, int bytes) {
+  int dev = 0;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  check_device(dev);
+  static std::map<std::pair<const void*, int>, int> done;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  int& have = done[std::make_pair(kernel, dev)];
+  if (have >= bytes) return;
+  C10_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  have = bytes;
 }
 
 // Read (and optionally clear) the first error code recorded by a bounded device wait.
@@ -98,6 +129,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gated_add_bwd", &osp::gated_add_bwd);
   m.def("qk_norm_rope_bwd", &osp::qk_norm_rope_bwd);
   m.def("gelu_tanh_bwd", &osp::gelu_tanh_bwd);
+  m.def("rms_norm_bwd", &osp::rms_norm_bwd);
   m.def("attention_fwd", &osp::attention_fwd);
   m.def("attention_bwd", &osp::attention_bwd);
   m.def("cfg_euler", &osp::cfg_euler);

@@ -358,12 +358,6 @@ constexpr int gemm_smem_bytes() {
   return 1024 + STAGES * (kBM * kBK * 2 + BN * kBK * 2) + (2 * STAGES + 5) * 8 + 16 + 128 + 8 * kStageBytes;
 }
 
-static int num_sms(int dev) {
-  static int cache[64] = {0};
-  if (!cache[dev]) cudaDeviceGetAttribute(&cache[dev], cudaDevAttrMultiProcessorCount, dev);
-  return cache[dev];
-}
-
 template <int BN, int MODE, typename OutT, bool A_MN = false, bool B_MN = false>
 static void launch_gemm(const at::Tensor& a, const at::Tensor& b, GemmArgs& args, cudaStream_t stream) {
   // K-major operand: rows of K elements (box 64 K × tile rows); MN-major: rows of M/N
@@ -374,11 +368,7 @@ static void launch_gemm(const at::Tensor& a, const at::Tensor& b, GemmArgs& args
                          : make_tmap_2d_bf16(b.data_ptr(), args.K, args.N, b.stride(0), kBK, BN);
   auto kern = gemm_kernel<BN, MODE, OutT, A_MN, B_MN>;
   constexpr int smem = gemm_smem_bytes<BN>();
-  static bool configured = false;
-  if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    configured = true;
-  }
+  smem_opt_in(reinterpret_cast<const void*>(kern), smem);
   const int tiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
   const int grid = std::max(1, std::min(tiles, num_sms(a.get_device())));
   kern<<<grid, kGemmThreads, smem, stream>>>(tmA, tmB, args);

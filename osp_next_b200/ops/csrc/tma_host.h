@@ -61,7 +61,16 @@ inline CUtensorMap make_tmap_2d_bf16(void* ptr, int64_t inner, int64_t outer, in
   return make_tmap_bf16(ptr, 2, dims, strides, box);
 }
 
+constexpr int kMaxDevices = 64;
+
 // One int per device; device code records the first error code (atomicCAS 0→code).
 int* error_word(int device);
+
+// Streaming multiprocessors of `device` (cached per device).
+int num_sms(int device);
+
+// Opt `kernel` into `bytes` of dynamic shared memory on the current device.  The
+// attribute is per device, so the setting is remembered per (kernel, device) pair.
+void smem_opt_in(const void* kernel, int bytes);
 
 }  // namespace osp

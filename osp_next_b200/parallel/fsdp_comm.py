@@ -14,10 +14,22 @@ every peer, and the collective is a tagged device barrier plus one pull kernel
 FSDP allocates these buffers in the same order on every rank, so the ring of slots
 gives a slot the same offset everywhere; the barrier checks that (it carries the
 offset as a tag) and the pull kernel does nothing if any peer disagrees or is late,
-recording an error code that :func:`check` raises on.  A slot is reused only
-``nslots`` collectives later, after every rank has passed the barriers in between, so
-no rank can overwrite a slot a peer is still reading.  Anything the arena cannot hold
-(another dtype, a larger buffer) goes to NCCL.
+recording an error code that :func:`check` (and the trainers' per-step check) raises on.
+
+Reusing a slot is ordered on the GPU, not only on the host.  Slot i of collective k is
+written again by collective k + nslots (FSDP's copy-in, on its copy-in stream).  Before
+that write the stream waits on two events of the slot:
+
+* ``peers_done``: recorded on the collective's stream right after the barrier of
+  collective k + 1 — every peer reaches that barrier only after its pull of collective k
+  (same stream), so no peer still reads slot i;
+* ``local_done``: recorded on the current stream when this rank drops its view of slot i
+  (FSDP drops it right after enqueuing its copy-out on that stream), so this rank's own
+  reads of the slot are ordered before the next write.
+
+The IPC views are outside PyTorch's caching allocator, so these events replace its
+stream tracking.  Anything the arena cannot hold (another dtype, a larger buffer) goes
+to NCCL.
 """
 from __future__ import annotations
 
@@ -35,8 +47,9 @@ from .. import ops
 class _Arena:
     """One IPC segment per rank split into ``nslots`` equal slots, plus a flag array."""
 
-    def __init__(self, group, slot_bytes: int, nslots: int, device):
+    def __init__(self, group, slot_bytes: int, nslots: int, device, barrier_limit_s: float = 60.0):
         self.group = group
+        self.barrier_limit_s = float(barrier_limit_s)
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.device = torch.device(device)
@@ -65,9 +78,21 @@ class _Arena:
         self.next = 0
         self.epoch = 0
         self.live: List[Optional[weakref.ref]] = [None] * nslots
+        self.peers_done: List[Optional[torch.cuda.Event]] = [None] * nslots
+        self.local_done: List[Optional[torch.cuda.Event]] = [None] * nslots
+        self._prev_slot: Optional[int] = None     # slot of the previous collective
         dist.barrier(group=group)
 
+    def _record_local_done(self, i: int):
+        def cb(_ref):
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self.device))
+            self.local_done[i] = ev
+        return cb
+
     def slot(self, numel: int, dtype: torch.dtype) -> Optional[torch.Tensor]:
+        """The next slot as a ``numel`` view; the current stream (FSDP's copy-in stream)
+        first waits until the slot's previous contents are no longer read anywhere."""
         nbytes = numel * torch.empty(0, dtype=dtype).element_size()
         if nbytes > self.slot_bytes:
             return None
@@ -76,17 +101,30 @@ class _Arena:
         if prev is not None and prev() is not None:
             raise RuntimeError("P2P FSDP arena: slot still in use; raise nslots")
         self.next = (i + 1) % self.nslots
+        stream = torch.cuda.current_stream(self.device)
+        for evs in (self.peers_done, self.local_done):
+            if evs[i] is not None:
+                stream.wait_event(evs[i])
+                evs[i] = None
         t = ops.ext().p2p_view(self.base + i * self.slot_bytes, [numel], dtype, self.device.index)
-        self.live[i] = weakref.ref(t)
+        self.live[i] = weakref.ref(t, self._record_local_done(i))
         return t
 
     def offset(self, t: torch.Tensor) -> Optional[int]:
         off = t.data_ptr() - self.base
         return off if 0 <= off < self.slot_bytes * self.nslots else None
 
-    def barrier(self, tag: int, limit_s: float = 2.0):
+    def barrier(self, tag: int, limit_s: Optional[float] = None):
+        """Tagged device barrier on the current stream; afterwards no peer reads the slot of
+        the previous collective any more (peers pull before they reach this barrier)."""
         self.epoch += 1
-        ops.ext().p2p_barrier_tagged(self.flag_ptrs, self.rank, self.world, self.epoch, int(tag), float(limit_s))
+        limit = self.barrier_limit_s if limit_s is None else float(limit_s)
+        ops.ext().p2p_barrier_tagged(self.flag_ptrs, self.rank, self.world, self.epoch, int(tag), limit)
+        if self._prev_slot is not None:
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self.device))
+            self.peers_done[self._prev_slot] = ev
+        self._prev_slot = int(tag) // self.slot_bytes
 
     def close(self):
         """Unmap the peers' segments, wait for every rank to do the same, free our own."""
@@ -156,11 +194,13 @@ def _group_shard_numel(module) -> int:
     return sum(fp.padded_sharded_param_size.numel() for fp in pg.fsdp_params) if pg is not None else 0
 
 
-def enable_p2p_fsdp(modules, group=None, nslots: int = 4, device=None):
+def enable_p2p_fsdp(modules, group=None, nslots: int = 4, device=None, barrier_limit_s: float = 60.0):
     """Route the parameter all-gather and gradient reduce-scatter of the given FSDP2
     modules (the transformer blocks) through the NVLink pull kernels.  All modules share
     one all-gather arena and one reduce-scatter arena sized for the largest of them.
-    Returns the two arenas (call :func:`close` on them at exit)."""
+    ``barrier_limit_s`` bounds each device barrier (a peer slower than that, e.g. stalled in
+    data loading, makes the collective give up and record an error that the trainer's
+    per-step check raises).  Returns the two arenas (call :func:`close` on them at exit)."""
     group = group or dist.group.WORLD
     world = dist.get_world_size(group)
     mods = [m for m in modules if hasattr(m, "set_custom_all_gather")]
@@ -168,8 +208,8 @@ def enable_p2p_fsdp(modules, group=None, nslots: int = 4, device=None):
         return None
     n = max(_group_shard_numel(m) for m in mods)
     dev = device or torch.device("cuda", torch.cuda.current_device())
-    ag = _Arena(group, n * world * 2, nslots, dev)        # bf16 parameters
-    rs = _Arena(group, n * world * 4, nslots, dev)        # fp32 gradients
+    ag = _Arena(group, n * world * 2, nslots, dev, barrier_limit_s)    # bf16 parameters
+    rs = _Arena(group, n * world * 4, nslots, dev, barrier_limit_s)    # fp32 gradients
     for m in mods:
         m.set_custom_all_gather(P2PAllGather(ag))
         m.set_custom_reduce_scatter(P2PReduceScatter(rs))

@@ -26,6 +26,7 @@ import torch.distributed as dist
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
+from osp_next_b200 import ops  # noqa: E402
 from osp_next_b200.data import ospnext_collators, ospnext_datasets, ospnext_samplers  # noqa: E402
 from osp_next_b200.engine import builders as B  # noqa: E402
 from osp_next_b200.parallel.checkpoint import Checkpointer  # noqa: E402
@@ -38,7 +39,8 @@ from osp_next_b200.utils.clip_grads import AdaptiveGradClipper  # noqa: E402
 from osp_next_b200.utils.config import load_config  # noqa: E402
 from osp_next_b200.utils.constant import PROMPT_IDS, PROMPT_MASK, VIDEO  # noqa: E402
 from osp_next_b200.utils.encoder_cache import EncoderCacheManager  # noqa: E402
-from osp_next_b200.utils.log_utils import get_logger, log_on_main_process  # noqa: E402
+from osp_next_b200.utils.log_utils import MetricsLogger, get_logger, log_on_main_process  # noqa: E402
+from osp_next_b200.utils.profiling import ProfileWindow, enable_nvtx, nvtx_range  # noqa: E402
 from osp_next_b200.utils.random_utils import set_deterministic, set_seed  # noqa: E402
 from osp_next_b200.utils.utils import to_dtype  # noqa: E402
 
@@ -92,7 +94,8 @@ def main(config, on_step=None):
         # block parameter all-gather / gradient reduce-scatter over NVLink peer memory
         from osp_next_b200.parallel.fsdp_comm import enable_p2p_fsdp
         fsdp_dim = mesh["fsdp"] if "ddp" in (mesh.mesh_dim_names or ()) else mesh
-        p2p_arenas = enable_p2p_fsdp(list(model.blocks), fsdp_dim.get_group(), device=dev)
+        p2p_arenas = enable_p2p_fsdp(list(model.blocks), fsdp_dim.get_group(), device=dev,
+                                     barrier_limit_s=config.get("fsdp_p2p_timeout_s", 60.0))
     ema = FSDPEMAModel(model, config.get("ema_decay", 0.9999), config.get("ema_update_interval", 1)) \
         if config.get("ema_decay", 0) else None
     opt = FusedAdamW([p for p in model.parameters() if p.requires_grad], lr=opt_cfg.get("lr", 1e-5),
@@ -142,6 +145,13 @@ def main(config, on_step=None):
     it_data = iter(loader)
 
     metrics_file = config.get("metrics_file")
+    wb = config.get("wandb_config", {}) or {}
+    metrics = MetricsLogger(metrics_file, use_wandb=wb.get("project_name") is not None,
+                            project=wb.get("project_name") or "osp_next_b200", run_name=wb.get("exp_name"),
+                            config=config)
+    profile = ProfileWindow(config.get("profiling", False), output_dir, rank)
+    if config.get("nvtx", False):
+        enable_nvtx(True)
     step_times, tokens_per_step = [], None
     model.train()
     it = start_it
@@ -149,29 +159,34 @@ def main(config, on_step=None):
         if dev.type == "cuda":
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record()
-        for micro in range(accum):
-            if cache.need_encode():
-                batch = next(it_data)
-                with torch.no_grad():
-                    if latent_mode:
-                        lat = batch["latents"].to(dev, non_blocking=True)
-                        txt = batch["text"].to(dev, non_blocking=True).to(weight_dtype)
-                    else:
-                        lat = vae.encode(batch[VIDEO].to(dev))
-                        txt = t5(batch[PROMPT_IDS].to(dev), batch[PROMPT_MASK].to(dev)).to(weight_dtype)
-                cache.set_cache([lat.float(), txt])
-            lat, txt = cache()
-            q = scheduler.q_sample(lat)
-            x_t, noise, sig, t = q["x_t"], q["prior_dist"], q["sigmas"], q["timesteps"]
-            _sp_broadcast([x_t, noise, sig, t], sp_rt.global_sp_group if gsp > 1 else None)
-            tokens_per_step = x_t.shape[0] * (x_t.shape[2] * x_t.shape[3] * x_t.shape[4] // 4) * W // max(1, gsp)
-            pred = model(x_t.to(weight_dtype), t, txt)
-            loss = scheduler.training_losses(pred, lat, noise, sigmas=sig)[0] / accum
-            loss.backward()
-        params = [p for p in model.parameters() if p.grad is not None]
-        opt.grad_scale = clipper.adaptive_clip(params, apply=False)
-        opt.step()
-        opt.zero_grad(set_to_none=True)
+        with profile(it):
+            for micro in range(accum):
+                with nvtx_range("data"):
+                    if cache.need_encode():
+                        batch = next(it_data)
+                        with torch.no_grad():
+                            if latent_mode:
+                                lat = batch["latents"].to(dev, non_blocking=True)
+                                txt = batch["text"].to(dev, non_blocking=True).to(weight_dtype)
+                            else:
+                                lat = vae.encode(batch[VIDEO].to(dev))
+                                txt = t5(batch[PROMPT_IDS].to(dev), batch[PROMPT_MASK].to(dev)).to(weight_dtype)
+                        cache.set_cache([lat.float(), txt])
+                    lat, txt = cache()
+                    q = scheduler.q_sample(lat)
+                    x_t, noise, sig, t = q["x_t"], q["prior_dist"], q["sigmas"], q["timesteps"]
+                    _sp_broadcast([x_t, noise, sig, t], sp_rt.global_sp_group if gsp > 1 else None)
+                tokens_per_step = x_t.shape[0] * (x_t.shape[2] * x_t.shape[3] * x_t.shape[4] // 4) * W // max(1, gsp)
+                with nvtx_range("forward"):
+                    pred = model(x_t.to(weight_dtype), t, txt)
+                    loss = scheduler.training_losses(pred, lat, noise, sigmas=sig)[0] / accum
+                with nvtx_range("backward"):
+                    loss.backward()
+        with nvtx_range("optimizer"):
+            params = [p for p in model.parameters() if p.grad is not None]
+            opt.grad_scale = clipper.adaptive_clip(params, apply=False)
+            opt.step()
+            opt.zero_grad(set_to_none=True)
         it += 1
         if ema is not None:
             ema.update(model, it)
@@ -182,6 +197,10 @@ def main(config, on_step=None):
             step_times.append(ms)
             if on_step is not None:
                 on_step(it, ms, tokens_per_step)
+        # a bounded device wait that gave up (a stalled or dead peer in an NVLink collective)
+        # leaves this step's gradients invalid: stop every rank before logging or saving;
+        # a restart resumes from the newest checkpoint
+        ops.check_device_errors_all_ranks(dev, where=f"training iteration {it}")
         if it % log_interval == 0:
             lv = gather_data_from_all_ranks(loss.detach().float() * accum).mean().item()
             ms_max = step_times[-1] if step_times else 0.0
@@ -194,16 +213,18 @@ def main(config, on_step=None):
                    "step_ms": ms_max,
                    "tokens_per_s": (tokens_per_step / (ms_max / 1000.0)) if ms_max else None}
             log_on_main_process(logger, json.dumps(rec))
-            if metrics_file and rank == 0:
-                with open(metrics_file, "a") as f:
-                    f.write(json.dumps(rec) + "\n")
+            metrics.log(dict(rec, **{f"clipper/{k}": v for k, v in clipper.state_dict().items()
+                                     if isinstance(v, (int, float))}), step=it)
         if it % save_interval == 0:
             ckpt.save(it, model, opt, ema, sampler, clipper)
+        if profile.finished(it):
+            log_on_main_process(logger, f"profiling window done at iteration {it}; traces in {output_dir}")
+            break
     if p2p_arenas is not None:
-        from osp_next_b200.parallel.fsdp_comm import check, close
-        check(p2p_arenas, dev.index)
+        from osp_next_b200.parallel.fsdp_comm import close
         dist.barrier()
         close(p2p_arenas)
+    metrics.close()
     return step_times
 
 
