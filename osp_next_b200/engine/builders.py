@@ -89,12 +89,17 @@ def build_vae(config, dev=None):
     return WanVAE(vae_pth=vc.get("vae_path"), dtype=to_dtype(vc.get("dtype", "fp32")), device=dev or device())
 
 
-def build_text_encoder(config, dev=None):
+def build_text_encoder(config, dev=None, mesh=None):
+    """umT5 encoder; with ``text_encoder_config.use_fsdp`` it is FSDP2-sharded over ``mesh``
+    (default: 8-way shards replicated over the rest of the world, as the reference)."""
     tc = config.get("text_encoder_config", {})
-    from ..models.t5 import T5EncoderModel
+    from ..models.t5 import T5EncoderModel, t5_mesh
+    use_fsdp = bool(tc.get("use_fsdp", False)) and dist.is_initialized() and world() > 1
+    if use_fsdp and mesh is None:
+        mesh = t5_mesh(world(), tc.get("fsdp_shard_size", 8), "cuda" if torch.cuda.is_available() else "cpu")
     return T5EncoderModel(text_len=tc.get("text_len", 512), dtype=to_dtype(tc.get("dtype", "bf16")),
                           device=dev or device(), checkpoint_path=tc.get("checkpoint_path"),
-                          tokenizer_path=tc.get("text_tokenizer_path"))
+                          tokenizer_path=tc.get("text_tokenizer_path"), use_fsdp=use_fsdp, device_mesh=mesh)
 
 
 def fsdp_wrap(model, config, mesh, weight_dtype=torch.bfloat16):

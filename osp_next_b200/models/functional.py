@@ -10,7 +10,8 @@ Three paths, chosen per call:
 * CUDA with autograd (training): :class:`torch.autograd.Function` wrappers whose
   forward runs the same kernels; GEMM backward runs on the same tcgen05 GEMM
   (reading dY, W and X MN-major in place); attention backward on its own tcgen05
-  kernels; norm/RoPE backward is written in PyTorch.
+  kernels; LN-modulate, RMSNorm, q/k-norm + RoPE, gated residual and GELU backward on
+  fused kernels (``ops/csrc/train_ops.cu``).
 """
 from __future__ import annotations
 
@@ -239,14 +240,48 @@ def layer_norm(x, weight, bias, eps):
     return F.layer_norm(x.float(), (x.shape[-1],), w, b, eps).to(_BF16)
 
 
+class _RMSNormFn(torch.autograd.Function):
+    """bf16 full-row RMSNorm with an fp32 weight, fused forward and backward kernels."""
+
+    @staticmethod
+    def forward(ctx, x, weight, eps):
+        xb = x.to(_BF16).contiguous()
+        ctx.save_for_backward(xb, weight)
+        ctx.eps = eps
+        ctx.x_dtype = x.dtype
+        return ops.rms_norm(xb, weight, eps)
+
+    @staticmethod
+    def backward(ctx, dy):
+        xb, w = ctx.saved_tensors
+        dx, dw = ops.rms_norm_bwd(xb, dy, w, ctx.eps)
+        return dx.to(ctx.x_dtype), (dw.to(w.dtype) if w is not None else None), None
+
+
 def rms_norm(x, weight, eps):
     if not x.is_cuda:
         xf = x.float()
         return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).type_as(x) * weight
     if _fused(x, weight):
         return ops.rms_norm(x, weight, eps)
+    if x.shape[-1] % 4 == 0 and x.shape[-1] <= 8192:
+        return _RMSNormFn.apply(x, weight, eps)
     xf = x.float()
     return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)) * weight.float()
+
+
+def qk_norm_rope_packed(qkv, wq, wk, pos, freqs, num_heads: int, eps: float):
+    """q/k RMSNorm + RoPE on a [B, n, 3C] qkv from any projection (plain, LoRA or HiF8
+    Linears): the fused kernel in place without autograd, else the kernel-backed autograd
+    function.  Returns (q, k, v) [B, n, H, D]."""
+    B, n, C3 = qkv.shape
+    C = C3 // 3
+    D = C // num_heads
+    if _fused(qkv, wq, wk):
+        return ops.qk_norm_rope(qkv.to(_BF16).contiguous(), wq, wk, pos, freqs, num_heads, eps)
+    out = _QKNormRopeFn.apply(qkv.to(_BF16), wq, wk, pos, freqs, num_heads, eps)
+    q, k, v = out.split(C, dim=-1)
+    return q.reshape(B, n, num_heads, D), k.reshape(B, n, num_heads, D), v.reshape(B, n, num_heads, D)
 
 
 def apply_rope(x, pos, freqs):

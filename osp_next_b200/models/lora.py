@@ -132,12 +132,23 @@ class LoraModel(nn.Module):
                 m.disabled = False
 
     def lora_state_dict(self) -> Dict[str, torch.Tensor]:
-        return {n: p.detach() for n, p in self.named_parameters() if "lora_" in n}
+        """LoRA parameters as full tensors.  Under FSDP2 the parameters are sharded DTensors
+        and gathering them is a collective: every rank of the mesh must call this."""
+        out = {}
+        for n, p in self.named_parameters():
+            if "lora_" in n:
+                t = p.detach()
+                out[n] = t.full_tensor() if hasattr(t, "full_tensor") else t
+        return out
 
-    def save_pretrained(self, path: str):
+    def save_pretrained(self, path: str, write: bool = True):
+        """Write ``adapter_model.bin`` + ``adapter_config.json`` (PEFT layout).  Call on every
+        rank when the model is FSDP-sharded; only ranks with ``write`` touch the disk."""
+        sd = {k: v.cpu().clone() for k, v in self.lora_state_dict().items()}
+        if not write:
+            return
         os.makedirs(path, exist_ok=True)
-        torch.save({k: v.cpu().clone() for k, v in self.lora_state_dict().items()},
-                   os.path.join(path, "adapter_model.bin"))
+        torch.save(sd, os.path.join(path, "adapter_model.bin"))
         with open(os.path.join(path, "adapter_config.json"), "w") as f:
             json.dump(self.peft_config["default"], f, indent=2)
 

@@ -172,11 +172,32 @@ def umt5_xxl(**overrides) -> T5Encoder:
     return T5Encoder(**cfg)
 
 
+def shard_t5(model: nn.Module, mesh=None) -> nn.Module:
+    """FSDP2-shard the frozen encoder: every T5SelfAttention layer, then the root
+    (reference: ospnext/modules/t5.py:500-506).  ``mesh`` is a (replicate, shard) mesh
+    (8-way shards by default, see :func:`t5_mesh`) or None for the default world mesh."""
+    from torch.distributed.fsdp import fully_shard
+    for m in model.modules():
+        if isinstance(m, T5SelfAttention):
+            fully_shard(m, mesh=mesh)
+    fully_shard(model, mesh=mesh)
+    return model
+
+
+def t5_mesh(world_size: int, shard: int = 8, device_type: str = "cuda"):
+    """(replicate, shard) mesh for the text encoder: shards of ``shard`` ranks (fewer when
+    the world is smaller), replicated over the rest (reference: train_osp.py:189-193)."""
+    from torch.distributed.device_mesh import init_device_mesh
+    n_rep = max(world_size // shard, 1)
+    return init_device_mesh(device_type, (n_rep, world_size // n_rep), mesh_dim_names=("replicate", "shard"))
+
+
 class T5EncoderModel:
     """Tokenise + encode prompts → ``[B, text_len, 4096]`` with zeros past each length."""
 
     def __init__(self, text_len=512, dtype=torch.bfloat16, device="cuda", checkpoint_path=None, tokenizer_path=None,
-                 shard_fn=None, encoder: Optional[T5Encoder] = None, tokenizer=None):
+                 shard_fn=None, encoder: Optional[T5Encoder] = None, tokenizer=None, use_fsdp: bool = False,
+                 device_mesh=None):
         self.text_len = text_len
         self.dtype = dtype
         self.device = device
@@ -185,6 +206,8 @@ class T5EncoderModel:
         if checkpoint_path:
             sd = torch.load(checkpoint_path, map_location="cpu", weights_only=True)
             model.load_state_dict(sd)
+        if use_fsdp and shard_fn is None:
+            shard_fn = lambda m: shard_t5(m.to(device=device, dtype=dtype), device_mesh)  # noqa: E731
         self.model = shard_fn(model) if shard_fn is not None else model.to(device=device, dtype=dtype)
         if tokenizer is None and tokenizer_path:
             from .tokenizers import HuggingfaceTokenizer

@@ -20,6 +20,7 @@ enum : int {
   kErrNone = 0,
   kErrGemmProducer = 101, kErrGemmMma = 102, kErrGemmEpilogue = 103, kErrGemmTeardown = 104,
   kErrAttnProducer = 201, kErrAttnMma = 202, kErrAttnSoftmax = 203, kErrAttnTeardown = 204,
+  kErrAttnLayout = 205,
   kErrP2P = 301, kErrP2PTag = 302,
   kErrProbeMbar = 901, kErrProbeFlag = 902,
 };
@@ -58,6 +59,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok) : "r"(addr), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Non-blocking probe: true once phase `parity` of `bar` has completed.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
   return ok != 0;
 }
 // Bounded wait for phase `parity` of `bar`. False (and an error code) on timeout.
@@ -196,7 +207,17 @@ __device__ __forceinline__ void tmem_st4(uint32_t taddr, uint32_t r0, uint32_t r
   asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};"
                :: "r"(taddr), "r"(r0), "r"(r1), "r"(r2), "r"(r3) : "memory");
 }
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+               :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+                  "r"(r[7]) : "memory");
+}
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Named barrier `id` (1..15) over `nthreads` threads (a multiple of 32).
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
+}
 
 // generic-proxy smem writes → visible to the async proxy (UMMA / TMA reads)
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -8,6 +8,7 @@
 //   gated_add_fwd/bwd out = resid + y·gate[b]            →  dy = dout·gate, Σ_rows dout·y
 //   qk_norm_rope_bwd  full-row RMSNorm(q)·w then 3-D RoPE →  d(raw q), Σ_rows (per-column dw)
 //   gelu_tanh_bwd     h = gelu_tanh(pre)                  →  dpre
+//   rms_norm_bwd      y = x·rsqrt(mean(x²)+eps)·w (row)   →  dx, Σ_rows dy·x̂
 //
 // Column reductions (gradients of per-batch modulation vectors and of norm weights) are
 // written as per-CTA partial sums [B, chunks, C] that the caller sums over chunks, so the
@@ -307,6 +308,74 @@ __global__ void gelu_tanh_bwd_kernel(const __nv_bfloat16* __restrict__ dh, const
   }
 }
 
+// ---------------------------------------------------------------------------- RMSNorm
+// y = x̂·w, x̂ = x·rstd, rstd = rsqrt(mean(x²) + eps) over rows of C.
+// dx = rstd·(g − x̂·mean(g·x̂)) with g = dy·w;  dw_part[chunk] = Σ_rows dy·x̂.
+// x, dy bf16 [rows, C]; dx bf16; grid ceil(rows / R).
+template <int MAXV>
+__global__ void __launch_bounds__(kThreads)
+rms_norm_bwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ dy,
+                    const float* __restrict__ w, __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_part,
+                    int rows, int C, float eps) {
+  __shared__ float2 red[kThreads / 32];
+  const int r0 = blockIdx.x * kRowsPerCta;
+  const int r1 = min(rows, r0 + kRowsPerCta);
+  const int nv = C / 4;
+  float4 wv[MAXV], acc[MAXV];
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int c4 = threadIdx.x + i * kThreads;
+    wv[i] = c4 < nv ? (w ? ld4(w + 4 * c4) : f4(1.f)) : f4(0.f);
+    acc[i] = f4(0.f);
+  }
+  const float inv_c = 1.0f / C;
+  for (int r = r0; r < r1; ++r) {
+    const long off = (long)r * C;
+    float4 xv[MAXV], g[MAXV];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int c4 = threadIdx.x + i * kThreads;
+      if (c4 < nv) {
+        xv[i] = ld4(x + off + 4 * c4);
+        ss += dot4(xv[i], xv[i]);
+      }
+    }
+    const float rstd = rsqrtf(block_sum2(ss, 0.f, red).x * inv_c + eps);
+    float sgx = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int c4 = threadIdx.x + i * kThreads;
+      if (c4 < nv) {
+        xv[i] = mul4(xv[i], f4(rstd));                         // x̂
+        const float4 d = ld4(dy + off + 4 * c4);
+        acc[i] = add4(acc[i], mul4(d, xv[i]));
+        g[i] = mul4(d, wv[i]);
+        sgx += dot4(g[i], xv[i]);
+      }
+    }
+    const float mgx = block_sum2(sgx, 0.f, red).x * inv_c;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int c4 = threadIdx.x + i * kThreads;
+      if (c4 < nv) {
+        float4 o;
+        o.x = rstd * (g[i].x - xv[i].x * mgx);
+        o.y = rstd * (g[i].y - xv[i].y * mgx);
+        o.z = rstd * (g[i].z - xv[i].z * mgx);
+        o.w = rstd * (g[i].w - xv[i].w * mgx);
+        st4(dx + off + 4 * c4, o);
+      }
+    }
+  }
+  const long poff = (long)blockIdx.x * C;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int c4 = threadIdx.x + i * kThreads;
+    if (c4 < nv) st4(dw_part + poff + 4 * c4, acc[i]);
+  }
+}
+
 }  // namespace trn
 
 #define OSP_TRN_DISPATCH(C, ...)                                           \
@@ -434,6 +503,34 @@ void gelu_tanh_bwd(const at::Tensor& dh, const at::Tensor& pre, at::Tensor& dpre
   trn::gelu_tanh_bwd_kernel<<<ew_blocks(total4), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(dh.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(pre.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(dpre.data_ptr()), total4);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// x, dy bf16 [rows, C] contiguous, w fp32 [C] (or undefined) → dx bf16, dw_part fp32 [chunks(rows), C]
+void rms_norm_bwd(const at::Tensor& x, const at::Tensor& dy, const c10::optional<at::Tensor>& w, at::Tensor& dx,
+                  at::Tensor& dw_part, double eps) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && dy.scalar_type() == at::kBFloat16 &&
+              dx.scalar_type() == at::kBFloat16 && x.is_contiguous() && dy.is_contiguous() && dx.is_contiguous(),
+              "rms_norm_bwd: contiguous bf16 x, dy, dx");
+  const int C = (int)x.size(-1);
+  const long rows = x.numel() / C;
+  TORCH_CHECK(C % 4 == 0 && dy.numel() == x.numel() && dx.numel() == x.numel(), "rms_norm_bwd: shapes");
+  TORCH_CHECK(dw_part.scalar_type() == at::kFloat && dw_part.is_contiguous() &&
+              dw_part.numel() == (long)chunks((int)rows) * C, "rms_norm_bwd: dw_part [chunks, C] fp32");
+  const float* wp = nullptr;
+  if (w.has_value() && w->defined()) {
+    TORCH_CHECK(w->scalar_type() == at::kFloat && w->is_contiguous() && w->numel() == C, "rms_norm_bwd: w fp32 [C]");
+    wp = w->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard guard(x.device());
+  if (rows == 0) return;
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int grid = chunks((int)rows);
+  OSP_TRN_DISPATCH(C, (trn::rms_norm_bwd_kernel<MV><<<grid, trn::kThreads, 0, st>>>(
+                          reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                          reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), wp,
+                          reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), dw_part.data_ptr<float>(), (int)rows, C,
+                          (float)eps)));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -83,3 +83,37 @@ def test_sp_matches_single_process(cfg_name, ssp, ul, shape):
     for n, g in g1.items():
         s = sum(o["grads"][n] for o in outs)
         assert torch.allclose(s, world * g, atol=1e-4, rtol=1e-3), (n, (s - world * g).abs().max())
+
+
+def _t5_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from osp_next_b200.models import t5 as mt5
+    torch.manual_seed(0)
+    enc = mt5.T5Encoder(vocab=100, dim=64, dim_attn=64, dim_ffn=128, num_heads=4, num_layers=2, num_buckets=32,
+                        shared_pos=False, dropout=0.0).eval()
+    ref = {k: v.clone() for k, v in enc.state_dict().items()}
+    model = mt5.T5EncoderModel(text_len=20, dtype=torch.float32, device="cpu", encoder=enc, use_fsdp=True,
+                               device_mesh=mt5.t5_mesh(world, 8, "cpu"))
+    assert any(hasattr(p, "to_local") for p in model.model.parameters())      # sharded
+    ids = torch.randint(0, 100, (2, 20), generator=torch.Generator().manual_seed(3))
+    m = torch.ones(2, 20, dtype=torch.long)
+    m[1, 12:] = 0
+    y = model(ids, m)
+    torch.save({"y": y, "ref": ref, "ids": ids, "m": m}, os.path.join(out_dir, f"t5_{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_t5_fsdp_sharded_encoder_matches_unsharded():
+    from osp_next_b200.models import t5 as mt5
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_t5_worker, args=(2, _port(), d), nprocs=2, join=True, start_method="spawn")
+        outs = [torch.load(os.path.join(d, f"t5_{r}.pt")) for r in range(2)]
+    enc = mt5.T5Encoder(vocab=100, dim=64, dim_attn=64, dim_ffn=128, num_heads=4, num_layers=2, num_buckets=32,
+                        shared_pos=False, dropout=0.0).eval()
+    enc.load_state_dict(outs[0]["ref"])
+    single = mt5.T5EncoderModel(text_len=20, dtype=torch.float32, device="cpu", encoder=enc)
+    exp = single(outs[0]["ids"], outs[0]["m"])
+    for o in outs:
+        assert torch.allclose(o["y"], exp, atol=1e-5), (o["y"] - exp).abs().max()

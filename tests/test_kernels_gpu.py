@@ -458,3 +458,74 @@ def test_training_affine_layer_norm_grads():
     for a, e in zip(got, (x.grad, w.grad, b.grad)):
         assert _rel(a, e) < 1e-2, _rel(a, e)
     _no_device_error()
+
+
+def test_training_rms_norm_grads():
+    """RMSNorm autograd on the fused forward/backward kernels vs the fp32 reference."""
+    from osp_next_b200.models import functional as Fn
+    torch.manual_seed(25)
+    for B, n, C in ((2, 77, 1024), (1, 512, 5120), (3, 5, 256)):
+        x = torch.randn(B, n, C, device=DEV).to(torch.bfloat16).requires_grad_(True)
+        w = (1 + 0.1 * torch.randn(C, device=DEV)).requires_grad_(True)
+        g = torch.randn(B, n, C, device=DEV)
+        (Fn._RMSNormFn.apply(x, w, 1e-6).float() * g).sum().backward()
+        got = (x.grad.clone(), w.grad.clone())
+        x.grad = w.grad = None
+        xf = x.float()
+        exp = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * w
+        (exp * g).sum().backward()
+        for a, e in zip(got, (x.grad, w.grad)):
+            assert _rel(a, e) < 1e-2, _rel(a, e)
+    _no_device_error()
+
+
+def test_lora_qkv_and_cross_attention_use_kernel_norms_with_matching_grads():
+    """With LoRA on q/k/v (self and cross attention) the q/k RMSNorm and RoPE run on the
+    fused kernels under autograd; the LoRA gradients match the fp32 CPU path."""
+    from osp_next_b200.models.lora import LoraModel
+    from osp_next_b200.models.osp_next import OSPNextModel
+    torch.manual_seed(0)
+    cfg = dict(dim=256, ffn_dim=512, num_heads=2, num_layers=2, text_len=16, skiparse_model_type="dual_end",
+               sparse_ratio=2, num_full_blocks=0)
+    targets = ["self_attn.q", "self_attn.k", "self_attn.v", "cross_attn.q", "cross_attn.k"]
+    m_cpu = LoraModel(OSPNextModel(**cfg), r=8, lora_alpha=8, target_modules=targets)
+    with torch.no_grad():
+        m_cpu.model.head.head.weight.normal_(std=0.02)
+        for mod in m_cpu.lora_modules():
+            mod.lora_B["default"].weight.normal_(std=0.02)
+    m_gpu = LoraModel(OSPNextModel(**cfg), r=8, lora_alpha=8, target_modules=targets).to(DEV)
+    m_gpu.load_state_dict(m_cpu.state_dict())
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(1, 16, 3, 16, 16, generator=g)
+    t = torch.tensor([400.0])
+    ctx = torch.randn(1, 16, 4096, generator=g)
+    tgt = torch.randn(1, 16, 3, 16, 16, generator=g)
+    calls = {"rms": 0, "qk": 0}
+    from osp_next_b200.models import functional as Fn
+    orig_rms, orig_qk = Fn._RMSNormFn.apply, Fn._QKNormRopeFn.apply
+
+    def rms(*a):
+        calls["rms"] += 1
+        return orig_rms(*a)
+
+    def qk(*a):
+        calls["qk"] += 1
+        return orig_qk(*a)
+    Fn._RMSNormFn.apply, Fn._QKNormRopeFn.apply = rms, qk
+    try:
+        for m, dev in ((m_cpu, "cpu"), (m_gpu, DEV)):
+            m.train()
+            loss = (m(x.to(dev), t.to(dev), ctx.to(dev)).float() - tgt.to(dev)).pow(2).mean()
+            loss.backward()
+    finally:
+        Fn._RMSNormFn.apply, Fn._QKNormRopeFn.apply = orig_rms, orig_qk
+    assert calls["qk"] >= 2 and calls["rms"] >= 2, calls
+    bad = []
+    for (n, pc), (_, pg) in zip(m_cpu.named_parameters(), m_gpu.named_parameters()):
+        if "lora_" not in n or pc.grad is None or pc.grad.norm() == 0:
+            continue
+        rel = ((pg.grad.cpu().float() - pc.grad).norm() / pc.grad.norm()).item()
+        if rel > 5e-2:
+            bad.append((n, rel))
+    assert not bad, bad
+    _no_device_error()
