@@ -50,17 +50,24 @@ def latent_mlp_score(device, seed: int = 0, channels: int = 16):
     return _fn
 
 
-def videoalign_score(device, load_from_pretrained=None, reward_dim="Overall", use_norm=True, save_fps=8,
-                     num_frames=None, fps=None, max_pixels=None, **kw):
+def videoalign_score(device, load_from_pretrained=None, load_from_pretrained_step=-1, reward_dim="Overall",
+                     use_norm=True, save_fps=8, num_frames=None, fps=None, max_pixels=None, **kw):
     from .videoalign import VideoAlignScorer
-    scorer = VideoAlignScorer(device=device, load_from_pretrained=load_from_pretrained, reward_dim=reward_dim,
-                              use_norm=use_norm, num_frames=num_frames, fps=fps, max_pixels=max_pixels)
+    scorer = VideoAlignScorer(device=device, load_from_pretrained=load_from_pretrained,
+                              load_from_pretrained_step=load_from_pretrained_step, reward_dim=reward_dim,
+                              use_norm=use_norm, num_frames=num_frames, fps=fps, max_pixels=max_pixels,
+                              save_fps=save_fps)
 
     def _fn(images, prompts, metadata):
         if isinstance(images, torch.Tensor):
-            if images.dim() == 5 and images.shape[1] == 3:           # [B, C, T, H, W] in [0,1]
+            if images.dim() == 5 and images.shape[1] == 3:           # [B, C, T, H, W] → [B, T, H, W, C]
                 images = images.permute(0, 2, 3, 4, 1)
-            images = (images * 255).round().clamp(0, 255).to(torch.uint8).cpu().numpy()
+            if images.dtype != torch.uint8:
+                x = images.float()
+                if x.min() < 0:                                       # VAE output in [-1, 1]
+                    x = (x + 1) * 0.5
+                images = (x * 255).round().clamp(0, 255).to(torch.uint8)
+            images = [v.cpu() for v in images]
         return scorer(images, prompts), {}
     return _fn
 
