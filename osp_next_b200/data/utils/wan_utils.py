@@ -147,7 +147,9 @@ class WanVideoProcessor:
         self.train_fps, self.sample_stride = train_fps, sample_stride
         if train_fps is None and sample_stride is None:
             raise ValueError("Must specify either train_fps or sample_stride")
-        self.transforms = Compose([CenterCropResizeVideo((self.h, self.w)), ToTensorAfterResize(), AENorm()])
+        self.transforms = Compose([CenterCropResizeVideo((self.h, self.w), interpolation_mode="bicubic",
+                                                         align_corners=False, antialias=True),
+                                   ToTensorAfterResize(), AENorm()])
         self.temporal_sample = TemporalRandomCrop(self.f, force_cut_video_from_start)
 
     def read_one_sample(self, path, meta: Optional[Dict] = None) -> torch.Tensor:

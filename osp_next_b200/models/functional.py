@@ -193,6 +193,17 @@ def gated_residual_linear(x, w, b, resid, gate=None):
     return resid.float() + (y * gate.float()[:, None, :] if gate is not None else y)
 
 
+def gated_add(resid, y, gate=None):
+    """resid + y·gate[b] for a branch output y produced outside the fused GEMM epilogue
+    (LoRA / HiF8 projections): the fused forward/backward kernels on CUDA."""
+    if (not resid.is_cuda or resid.dtype != torch.float32 or resid.dim() != 3 or y.shape[-1] % 4
+            or y.shape != resid.shape):
+        return resid + (y * gate[:, None, :] if gate is not None else y)
+    if _fused(resid, y, gate):
+        return ops.gated_add(resid, y, gate)
+    return _GatedAddFn.apply(resid, y.to(_BF16), gate)
+
+
 # ----------------------------------------------------------------------------- norms
 
 def ln_modulate(x, shift, scale, eps):

@@ -139,9 +139,14 @@ class OSPNextSelfAttention(nn.Module):
                                     (self.q.bias, self.k.bias, self.v.bias), self.norm_q(None, weight_only=True),
                                     self.norm_k(None, weight_only=True), ctx.pos, ctx.freqs, H, self.eps)
         if x.is_cuda and self.qk_norm and ctx.pos is not None and (D * H) % 4 == 0:
-            # wrapped projections (LoRA, HiF8) run their own forward; the q/k RMSNorm and the
-            # RoPE stay on the fused kernel (forward and backward) whatever the Linear type
-            qkv = torch.cat([_lin(self.q, x), _lin(self.k, x), _lin(self.v, x)], dim=-1)
+            # wrapped projections (LoRA, HiF8) run their own forward (HiF8: one quantisation of
+            # x and one GEMM for all three); the q/k RMSNorm and the RoPE stay on the fused
+            # kernel (forward and backward) whatever the Linear type
+            if _hif8(self) and all(getattr(m, "is_hif8", False) for m in (self.q, self.k, self.v)):
+                from ..quant.hif8 import hif8_multi_linear
+                qkv = hif8_multi_linear(x, (self.q, self.k, self.v))
+            else:
+                qkv = torch.cat([_lin(self.q, x), _lin(self.k, x), _lin(self.v, x)], dim=-1)
             wq = self.norm_q(None, weight_only=True) if torch.is_grad_enabled() else self.norm_q.weight
             wk = self.norm_k(None, weight_only=True) if torch.is_grad_enabled() else self.norm_k.weight
             return Fn.qk_norm_rope_packed(qkv, wq, wk, ctx.pos, ctx.freqs, H, self.eps)
@@ -246,17 +251,20 @@ class OSPNextAttentionBlock(nn.Module):
         xm = Fn.ln_modulate(x, e[0], e[1], self.eps)
         y = self.self_attn(xm, ctx)
         x = Fn.gated_residual_linear(y, self.self_attn.o.weight, self.self_attn.o.bias, x, e[2]) \
-            if _plain(self.self_attn.o) else x + self.self_attn.o(y) * e[2][:, None, :]
+            if _plain(self.self_attn.o) else Fn.gated_add(x, self.self_attn.o(y), e[2])
         # cross-attention
         xn = self.norm3(x) if self.cross_attn_norm else (x if not x.is_cuda else x.to(torch.bfloat16))
         y = self.cross_attn(xn, text, text_kv)
         x = Fn.gated_residual_linear(y, self.cross_attn.o.weight, self.cross_attn.o.bias, x, None) \
-            if _plain(self.cross_attn.o) else x + self.cross_attn.o(y)
+            if _plain(self.cross_attn.o) else Fn.gated_add(x, self.cross_attn.o(y), None)
         # FFN
         xm = Fn.ln_modulate(x, e[3], e[4], self.eps)
         f0, f2 = self.ffn[0], self.ffn[2]
         if _plain(f0):
             h = Fn.linear(xm, f0.weight, f0.bias, act="gelu_tanh")
+        elif getattr(f0, "is_hif8", False):
+            from ..quant.hif8 import hif8_multi_linear
+            h = hif8_multi_linear(xm, (f0,), act="gelu_tanh")       # GELU in the GEMM epilogue
         else:
             h = self.ffn[1](f0(xm))
         if _plain(f2) and ctx.p2p is not None and Fn._fused(h, f2.weight, x):
@@ -273,7 +281,7 @@ class OSPNextAttentionBlock(nn.Module):
         if _plain(f2):
             x = Fn.gated_residual_linear(h, f2.weight, f2.bias, x, e[5])
         else:
-            x = x + f2(h) * e[5][:, None, :]
+            x = Fn.gated_add(x, f2(h), e[5])
         return x
 
     def forward(self, x, e0, text, ctx: BlockContext, text_kv=None, gradient_checkpointing=False):

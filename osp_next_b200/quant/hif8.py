@@ -66,6 +66,90 @@ class _HIF8LinearFunction(torch.autograd.Function):
         return dx.view(x_q.shape).to(x_q.dtype), dw.to(w_q.dtype), db, None, None
 
 
+class _HIF8MultiLinearFn(torch.autograd.Function):
+    """Several HiF8 Linears that read the same input (q/k/v, or one Linear with a GELU
+    epilogue): x is quantised once, each weight with its own per-tensor scale, and one
+    GEMM runs on the concatenated quantised weights.  Backward quantises each output
+    slice's gradient with its own scale (exactly what separate HIF8Linear modules do) and
+    runs dX and dW as one GEMM each over the packed slices.  CUDA only."""
+
+    @staticmethod
+    def forward(ctx, x, smf, smb, act, n, *wb):
+        ws, bs = wb[:n], wb[n:]
+        x_q = quant(x.to(torch.bfloat16).contiguous(), smf)
+        w_q = torch.cat([quant(w.detach().to(torch.bfloat16).contiguous(), smf) for w in ws], 0)
+        has_b = all(b is not None for b in bs)
+        b = torch.cat([b_.float() for b_ in bs], 0) if has_b else None
+        x2 = x_q.reshape(-1, x.shape[-1])
+        pre = None
+        if act == "gelu_tanh" and w_q.shape[0] % 32 == 0 and x2.shape[1] % 8 == 0:
+            y, pre = ops.linear_gelu_aux(x2, w_q, b)
+        elif act == "gelu_tanh":
+            pre = ops.linear(x2, w_q, b, None)
+            y = F.gelu(pre.float(), approximate="tanh").to(torch.bfloat16)
+        else:
+            y = ops.linear(x2, w_q, b, None)
+        ctx.save_for_backward(x_q, w_q, pre)
+        ctx.meta = (smb, act, [w.shape[0] for w in ws], [w.dtype for w in ws], has_b, x.dtype, x.shape)
+        return y.view(*x.shape[:-1], w_q.shape[0])
+
+    @staticmethod
+    def backward(ctx, gy):
+        x_q, w_q, pre = ctx.saved_tensors
+        smb, act, outs, wdts, has_b, xdt, xshape = ctx.meta
+        g = gy.reshape(-1, gy.shape[-1])
+        if act == "gelu_tanh":
+            g = ops.gelu_tanh_bwd(g, pre.to(torch.bfloat16)) if pre.dtype == torch.bfloat16 else \
+                torch.autograd.grad(F.gelu(pre.float().requires_grad_(True), approximate="tanh"), pre, g.float())[0]
+        # per-slice gradient quantisation (one scale per original Linear)
+        parts, o = [], 0
+        for n_out in outs:
+            parts.append(quant(g[:, o:o + n_out].contiguous().to(torch.bfloat16), smb))
+            o += n_out
+        gq = torch.cat(parts, 1) if len(parts) > 1 else parts[0]
+        x2 = x_q.reshape(-1, x_q.shape[-1])
+        dx = ops.gemm_t(gq, w_q, a_mn=False, b_mn=True)
+        if dx is None:
+            dx = ops.linear(gq, w_q.t().contiguous(), None, out_dtype=torch.float32)
+        dw = ops.gemm_t(gq, x2, a_mn=True, b_mn=True)
+        if dw is None:
+            dw = ops.linear(gq.t().contiguous(), x2.t().contiguous(), None, out_dtype=torch.float32)
+        dws = list(dw.split(outs, 0))
+        dbs = list(gq.float().sum(0).split(outs, 0)) if has_b else [None] * len(outs)
+        grads = [dx.view(xshape).to(xdt), None, None, None, None]
+        grads += [d.to(t) for d, t in zip(dws, wdts)] + dbs
+        return tuple(grads)
+
+
+def hif8_multi_linear(x, linears, act=None):
+    """y = [HIF8Linear_1(x) | … | HIF8Linear_n(x)] (optionally gelu_tanh of it) in one GEMM,
+    with the same quantisation semantics as calling each module.  ``linears`` share one
+    input and the scale settings of the first."""
+    l0 = linears[0]
+    smf, smb = l0.scale_max_forward, l0.scale_max_backward
+    if not x.is_cuda:
+        y = torch.cat([m(x) for m in linears], -1)
+        return F.gelu(y, approximate="tanh") if act == "gelu_tanh" else y
+    if not (torch.is_grad_enabled() and (x.requires_grad or any(m.weight.requires_grad for m in linears))):
+        x_q = quant(x.to(torch.bfloat16).contiguous(), smf)
+        if len(linears) == 1:
+            w_q = l0._cached_wq()
+        else:                        # packed quantised weights, rebuilt when any weight changes
+            key = tuple((m.weight.data_ptr(), m.weight._version) for m in linears)
+            hit = getattr(l0, "_packed_wq", None)
+            if hit is None or hit[0] != key:
+                hit = (key, torch.cat([m._cached_wq() for m in linears], 0))
+                l0._packed_wq = hit
+            w_q = hit[1]
+        bs = [m.bias for m in linears]
+        b = torch.cat([b_.float() for b_ in bs], 0) if all(b_ is not None for b_ in bs) else None
+        y = ops.linear(x_q.reshape(-1, x.shape[-1]), w_q, b, act)
+        return y.view(*x.shape[:-1], w_q.shape[0])
+    ws = [m.weight for m in linears]
+    bs = [m.bias for m in linears]
+    return _HIF8MultiLinearFn.apply(x, smf, smb, act, len(linears), *ws, *bs)
+
+
 class HIF8Linear(nn.Linear):
     """Drop-in ``nn.Linear`` with HiF8 fake quantisation of x, W (forward) and dY (backward)."""
     is_hif8 = True

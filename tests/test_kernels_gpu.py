@@ -529,3 +529,40 @@ def test_lora_qkv_and_cross_attention_use_kernel_norms_with_matching_grads():
             bad.append((n, rel))
     assert not bad, bad
     _no_device_error()
+
+
+def test_hif8_multi_linear_matches_separate_modules():
+    """One quantisation of the shared input + one GEMM over the packed quantised weights
+    (and the GELU epilogue) gives the same outputs and gradients as separate HIF8Linear
+    modules followed by GELU."""
+    from osp_next_b200.quant.hif8 import HIF8Linear, hif8_multi_linear
+    torch.manual_seed(26)
+    C, n = 256, 300
+    mods = [HIF8Linear(C, C).to(DEV) for _ in range(3)]
+    x = torch.randn(2, n, C, device=DEV).to(torch.bfloat16).requires_grad_(True)
+    y = hif8_multi_linear(x, mods)
+    g = torch.randn_like(y, dtype=torch.float32)
+    (y.float() * g).sum().backward()
+    got = [x.grad.clone()] + [m.weight.grad.clone() for m in mods] + [m.bias.grad.clone() for m in mods]
+    for t in [x] + [m.weight for m in mods] + [m.bias for m in mods]:
+        t.grad = None
+    y2 = torch.cat([m(x) for m in mods], -1)
+    (y2.float() * g).sum().backward()
+    exp = [x.grad] + [m.weight.grad for m in mods] + [m.bias.grad for m in mods]
+    assert _rel(y, y2) < 1e-2
+    for a, e in zip(got, exp):
+        assert _rel(a, e) < 2e-2, _rel(a, e)
+    # GELU epilogue variant vs Linear → GELU
+    f = HIF8Linear(C, 512).to(DEV)
+    h = hif8_multi_linear(x, (f,), act="gelu_tanh")
+    gh = torch.randn_like(h, dtype=torch.float32)
+    x.grad = None
+    (h.float() * gh).sum().backward()
+    got = (x.grad.clone(), f.weight.grad.clone())
+    x.grad = f.weight.grad = None
+    h2 = torch.nn.functional.gelu(f(x).float(), approximate="tanh")
+    (h2 * gh).sum().backward()
+    assert _rel(h, h2) < 2e-2
+    for a, e in zip(got, (x.grad, f.weight.grad)):
+        assert _rel(a, e) < 3e-2, _rel(a, e)
+    _no_device_error()
