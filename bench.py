@@ -182,7 +182,10 @@ def layout_for(world: int):
 
 # ----------------------------------------------------------------------------- our framework
 
-def run_ours(args, rank, world, local):
+def run_ours(args, rank, world, local, profile_hook=None):
+    """Time ``args.steps`` sampling steps (device events, max over ranks) and the public
+    pipeline end to end.  ``profile_hook(fn)``, when given, is called with a function that
+    runs the steps instead of timing them (analysis tools; no bench line)."""
     from osp_next_b200 import ops
     from osp_next_b200.models.osp_next import OSPNextModel
     from osp_next_b200.parallel.cfg import CFGParallel
@@ -228,6 +231,12 @@ def run_ours(args, rank, world, local):
     with torch.no_grad():
         device_steps(args.warmup)
         barrier_sync()
+        if profile_hook is not None:
+            profile_hook(lambda: device_steps(args.steps))
+            barrier_sync()
+            if getattr(getattr(model, "parallel", None), "p2p", None) is not None:
+                model.parallel.p2p.close()
+            return None
         clock = ClockSampler(local)
         clock.start()
         l0 = ops._ext.launch_count()

@@ -60,20 +60,83 @@ class LoraLinear(nn.Module):
             nn.init.normal_(self.lora_A[self.adapter].weight, std=1.0 / self.r)
             nn.init.zeros_(self.lora_B[self.adapter].weight)
 
-    def forward(self, x):
+    def forward(self, x, act=None):
+        if (x.is_cuda and not self.disabled and type(self.base_layer) is nn.Linear
+                and not self.base_layer.weight.requires_grad and torch.is_grad_enabled()):
+            # trainable adapter on a frozen base (RL / LoRA fine-tuning): one dual GEMM
+            return _LoraDualFn.apply(x, self.base_layer.weight, self.base_layer.bias,
+                                     self.lora_A[self.adapter].weight, self.lora_B[self.adapter].weight,
+                                     self.scaling, act)
         y = self.base_layer(x) if not isinstance(self.base_layer, nn.Linear) else \
             Fn.linear(x, self.base_layer.weight, self.base_layer.bias)
-        if self.disabled:
-            return y
-        a = Fn.linear(x, self.lora_A[self.adapter].weight)
-        b = Fn.linear(a, self.lora_B[self.adapter].weight)
-        return y + b.to(y.dtype) * self.scaling
+        if not self.disabled:
+            a = Fn.linear(x, self.lora_A[self.adapter].weight)
+            b = Fn.linear(a, self.lora_B[self.adapter].weight)
+            y = y + b.to(y.dtype) * self.scaling
+        return Fn.F.gelu(y, approximate="tanh") if act == "gelu_tanh" else y
 
     @torch.no_grad()
     def merged_weight(self):
         A = self.lora_A[self.adapter].weight.float()
         B = self.lora_B[self.adapter].weight.float()
         return (self.base_layer.weight.float() + self.scaling * (B @ A)).to(self.base_layer.weight.dtype)
+
+
+class _LoraDualFn(torch.autograd.Function):
+    """y = act(x·Wᵀ + b + s·(x·Aᵀ)·Bᵀ) for a frozen base W and trainable A [r, K], B [N, r]:
+    forward = the small GEMM a = x·Aᵀ and ONE GEMM with (a, s·B) as a second operand pair
+    (GELU in its epilogue when asked); backward with tcgen05 GEMMs:
+    g_a = s·gy·B, dA = g_aᵀ·x, dB = s·gyᵀ·a, dX = gy·W + g_a·A."""
+
+    @staticmethod
+    def forward(ctx, x, w, bias, A, Bm, scaling, act):
+        from .. import ops
+        shp = x.shape
+        x2 = x.reshape(-1, shp[-1]).to(torch.bfloat16)
+        a = ops.linear(x2, A.to(torch.bfloat16), None)                     # [M, r] bf16
+        sB = (Bm.float() * scaling).to(torch.bfloat16)
+        if act == "gelu_tanh":
+            y, pre = ops.linear_gelu_aux(x2, w, bias, extra=(a, sB))        # GELU in the epilogue
+        else:
+            pre = None
+            y = ops.linear(x2, w, bias, None, extra=(a, sB))
+        ctx.save_for_backward(x2, w, A, Bm, a, pre)
+        ctx.meta = (scaling, act, shp, x.dtype, bias is not None)
+        return y.view(*shp[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, gy):
+        from .. import ops
+        x2, w, A, Bm, a, pre = ctx.saved_tensors
+        s, act, shp, xdt, has_b = ctx.meta
+        g = gy.reshape(-1, gy.shape[-1])
+        if act == "gelu_tanh":
+            g = ops.gelu_tanh_bwd(g, pre)
+        gb = g.to(torch.bfloat16)
+        Bb = Bm.to(torch.bfloat16)
+        # g_a = s·g·B  [M, r]: B [N, r] read MN-major
+        g_a = ops.gemm_t(gb, Bb, a_mn=False, b_mn=True)
+        if g_a is None:
+            g_a = ops.linear(gb, Bb.t().contiguous(), None, out_dtype=torch.float32)
+        g_a = g_a * s
+        gab = g_a.to(torch.bfloat16)
+        dA = ops.gemm_t(gab, x2, a_mn=True, b_mn=True)
+        if dA is None:
+            dA = ops.linear(gab.t().contiguous(), x2.t().contiguous(), None, out_dtype=torch.float32)
+        dB = ops.gemm_t(gb, a, a_mn=True, b_mn=True)
+        if dB is None:
+            dB = ops.linear(gb.t().contiguous(), a.t().contiguous(), None, out_dtype=torch.float32)
+        dB = dB * s
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = ops.gemm_t(gb, w.to(torch.bfloat16), a_mn=False, b_mn=True)
+            if dx is None:
+                dx = ops.linear(gb, w.to(torch.bfloat16).t().contiguous(), None, out_dtype=torch.float32)
+            dxa = ops.gemm_t(gab, A.to(torch.bfloat16), a_mn=False, b_mn=True)
+            if dxa is None:
+                dxa = ops.linear(gab, A.to(torch.bfloat16).t().contiguous(), None, out_dtype=torch.float32)
+            dx = (dx.float() + dxa.float()).view(shp).to(xdt)
+        return dx, None, None, dA.to(A.dtype), dB.to(Bm.dtype), None, None
 
 
 def _match(name: str, targets: Iterable[str]) -> bool:
@@ -183,3 +246,57 @@ class LoraModel(nn.Module):
                     base.weight.copy_(child.merged_weight())
                     setattr(mod, cname, base)
         return model
+
+
+# ---------------------------------------------------------------------------- fused inference path
+_PACK_CACHE: Dict[tuple, tuple] = {}
+
+
+def _key(ts):
+    return tuple((t.data_ptr(), t._version) for t in ts if t is not None)
+
+
+def fused_lora_operands(mods, x2d: torch.Tensor):
+    """Operands of ONE GEMM computing ``[m_1(x) | … | m_n(x)]`` for Linears / LoraLinears that
+    share the input ``x2d`` [M, K]:  base weights concatenated [ΣN, K] + bias, and the LoRA
+    branches as a second operand pair ``(a2, b2)`` with ``a2 = x·[A_1; …]ᵀ`` [M, Σr] (one
+    small GEMM) and ``b2`` the block-diagonal of ``scaling_i·B_i`` [ΣN, Σr] — so the LoRA
+    update accumulates into the base GEMM's accumulator and every fused epilogue still
+    applies.  Returns (W, b, extra-or-None); no-grad use (rollouts, inference)."""
+    from .. import ops
+    base = [m.base_layer if isinstance(m, LoraLinear) else m for m in mods]
+    lora = [m for m in mods if isinstance(m, LoraLinear) and not m.disabled]
+    wkey = ("w",) + _key([b.weight for b in base] + [b.bias for b in base])
+    hit = _PACK_CACHE.get(wkey)
+    if hit is None:
+        W = torch.cat([b.weight.detach() for b in base], 0).to(torch.bfloat16).contiguous() if len(base) > 1 \
+            else base[0].weight.detach().to(torch.bfloat16).contiguous()
+        bs = [b.bias for b in base]
+        bias = torch.cat([b.detach().float() for b in bs], 0).contiguous() if all(b is not None for b in bs) else None
+        hit = (W, bias)
+        if len(_PACK_CACHE) > 512:
+            _PACK_CACHE.clear()
+        _PACK_CACHE[wkey] = hit
+    W, bias = hit
+    if not lora:
+        return W, bias, None
+    akey = ("a",) + tuple(id(m) for m in mods) + _key([m.lora_A[m.adapter].weight for m in lora] +
+                                                      [m.lora_B[m.adapter].weight for m in lora])
+    hit = _PACK_CACHE.get(akey)
+    if hit is None:
+        A = torch.cat([m.lora_A[m.adapter].weight.detach() for m in lora], 0).to(torch.bfloat16).contiguous()
+        rs = sum(m.r for m in lora)
+        Bd = torch.zeros(W.shape[0], rs, dtype=torch.bfloat16, device=W.device)
+        row = col = 0
+        for m in mods:
+            n_out = (m.base_layer if isinstance(m, LoraLinear) else m).weight.shape[0]
+            if isinstance(m, LoraLinear) and not m.disabled:
+                Bd[row:row + n_out, col:col + m.r] = (m.lora_B[m.adapter].weight.detach().float() * m.scaling).to(
+                    torch.bfloat16)
+                col += m.r
+            row += n_out
+        hit = (A, Bd)
+        _PACK_CACHE[akey] = hit
+    A, Bd = hit
+    a2 = ops.linear(x2d, A, None)
+    return W, bias, (a2, Bd)

@@ -132,6 +132,15 @@ class OSPNextSelfAttention(nn.Module):
             W, b = self.packed_qkv()
             qkv = Fn.ops.linear(x, W, b)
             return Fn.ops.qk_norm_rope(qkv, self.norm_q.weight, self.norm_k.weight, ctx.pos, ctx.freqs, H, self.eps)
+        if (lora and not _hif8(self) and self.qk_norm and ctx.pos is not None
+                and Fn._fused(x, self.q.weight, *[p for m in (self.q, self.k, self.v) for p in _lora_params(m)])):
+            # LoRA folded into the packed QKV GEMM (second operand pair), then the fused q/k
+            # norm + RoPE, as the plain path
+            from .lora import fused_lora_operands
+            x2 = x.reshape(-1, x.shape[-1])
+            W, b, extra = fused_lora_operands((self.q, self.k, self.v), x2)
+            qkv = Fn.ops.linear(x2, W, b, extra=extra).view(B, n, -1)
+            return Fn.ops.qk_norm_rope(qkv, self.norm_q.weight, self.norm_k.weight, ctx.pos, ctx.freqs, H, self.eps)
         if (x.is_cuda and self.qk_norm and not lora and not _hif8(self) and ctx.pos is not None
                 and all(type(m) is nn.Linear for m in (self.q, self.k, self.v))):
             # training: one QKV GEMM + fused q/k norm and RoPE with kernel backward
@@ -181,12 +190,46 @@ def _hif8(attn) -> bool:
     return getattr(attn.q, "is_hif8", False)
 
 
-def _lin(mod, x):
-    """Plain Linears go through the functional layer (fused GEMM / dtype handling);
-    wrapped ones (LoRA, HiF8) run their own forward."""
+def _lin(mod, x, act=None):
+    """Plain Linears go through the functional layer (fused GEMM / dtype handling); LoRA
+    Linears without autograd fold their branch into the same GEMM; other wrapped ones
+    (HiF8, LoRA under autograd) run their own forward."""
     if type(mod) is nn.Linear:
-        return Fn.linear(x, mod.weight, mod.bias)
-    return mod(x)
+        return Fn.linear(x, mod.weight, mod.bias, act=act)
+    if _lora_fusable(mod, x):
+        from .lora import fused_lora_operands
+        x2 = x.reshape(-1, x.shape[-1])
+        W, b, extra = fused_lora_operands((mod,), x2)
+        return Fn.ops.linear(x2, W, b, act=act, extra=extra).view(*x.shape[:-1], W.shape[0])
+    y = mod(x)
+    return Fn.F.gelu(y, approximate="tanh") if act == "gelu_tanh" else y
+
+
+def _lora_params(mod):
+    return [mod.lora_A[mod.adapter].weight, mod.lora_B[mod.adapter].weight] if hasattr(mod, "lora_A") else []
+
+
+def _lora_fusable(mod, x) -> bool:
+    """A LoRA Linear may take the folded no-grad GEMM only when no autograd graph is needed
+    through its input, its base weight or its LoRA factors."""
+    return (hasattr(mod, "lora_A") and type(mod.base_layer) is nn.Linear
+            and Fn._fused(x, mod.weight, *_lora_params(mod)))
+
+
+def _gated_out(mod, h, resid, gate, dest_row=None, n_out=None):
+    """resid + mod(h)·gate: plain and (no-grad) LoRA Linears on the gated-residual GEMM
+    epilogue (optionally storing rows in the next layout), others on the fused gated add."""
+    if _plain(mod):
+        if dest_row is not None:
+            return Fn.ops.linear_gated_residual(h, mod.weight, mod.bias, resid, gate, dest_row=dest_row, n_out=n_out)
+        return Fn.gated_residual_linear(h, mod.weight, mod.bias, resid, gate)
+    if _lora_fusable(mod, h) and resid.dtype == torch.float32 and Fn._fused(resid):
+        from .lora import fused_lora_operands
+        W, b, extra = fused_lora_operands((mod,), h.reshape(-1, h.shape[-1]))
+        out = resid if (dest_row is None and resid.is_contiguous()) else None
+        return Fn.ops.linear_gated_residual(h, W, b, resid, gate, dest_row=dest_row, n_out=n_out, out=out,
+                                            extra=extra)
+    return Fn.gated_add(resid, mod(h), gate)
 
 
 class OSPNextCrossAttention(OSPNextSelfAttention):
@@ -250,21 +293,21 @@ class OSPNextAttentionBlock(nn.Module):
         # self-attention
         xm = Fn.ln_modulate(x, e[0], e[1], self.eps)
         y = self.self_attn(xm, ctx)
-        x = Fn.gated_residual_linear(y, self.self_attn.o.weight, self.self_attn.o.bias, x, e[2]) \
-            if _plain(self.self_attn.o) else Fn.gated_add(x, self.self_attn.o(y), e[2])
+        x = _gated_out(self.self_attn.o, y, x, e[2])
         # cross-attention
         xn = self.norm3(x) if self.cross_attn_norm else (x if not x.is_cuda else x.to(torch.bfloat16))
         y = self.cross_attn(xn, text, text_kv)
-        x = Fn.gated_residual_linear(y, self.cross_attn.o.weight, self.cross_attn.o.bias, x, None) \
-            if _plain(self.cross_attn.o) else Fn.gated_add(x, self.cross_attn.o(y), None)
+        x = _gated_out(self.cross_attn.o, y, x, None)
         # FFN
         xm = Fn.ln_modulate(x, e[3], e[4], self.eps)
         f0, f2 = self.ffn[0], self.ffn[2]
-        if _plain(f0):
-            h = Fn.linear(xm, f0.weight, f0.bias, act="gelu_tanh")
-        elif getattr(f0, "is_hif8", False):
+        if getattr(f0, "is_hif8", False):
             from ..quant.hif8 import hif8_multi_linear
             h = hif8_multi_linear(xm, (f0,), act="gelu_tanh")       # GELU in the GEMM epilogue
+        elif _plain(f0) or _lora_fusable(f0, xm):
+            h = _lin(f0, xm, act="gelu_tanh")
+        elif hasattr(f0, "lora_A"):
+            h = f0(xm, act="gelu_tanh")                 # LoRA under autograd: GELU in the dual GEMM
         else:
             h = self.ffn[1](f0(xm))
         if _plain(f2) and ctx.p2p is not None and Fn._fused(h, f2.weight, x):
@@ -273,16 +316,11 @@ class OSPNextAttentionBlock(nn.Module):
             Fn.ops.linear_gated_residual_p2p(h, f2.weight, f2.bias, x, e[5], drank, drow, ptrs, stride)
             ctx.relaid = True
             return None
-        if _plain(f2) and ctx.next_dest_row is not None and Fn._fused(h, f2.weight, x):
+        if (_plain(f2) or _lora_fusable(f2, h)) and ctx.next_dest_row is not None and Fn._fused(h, f2.weight, x):
             # layout change for the next block fused into the FFN-down store
             ctx.relaid = True
-            return Fn.ops.linear_gated_residual(h, f2.weight, f2.bias, x, e[5],
-                                                dest_row=ctx.next_dest_row, n_out=ctx.next_n)
-        if _plain(f2):
-            x = Fn.gated_residual_linear(h, f2.weight, f2.bias, x, e[5])
-        else:
-            x = Fn.gated_add(x, f2(h), e[5])
-        return x
+            return _gated_out(f2, h, x, e[5], dest_row=ctx.next_dest_row, n_out=ctx.next_n)
+        return _gated_out(f2, h, x, e[5])
 
     def forward(self, x, e0, text, ctx: BlockContext, text_kv=None, gradient_checkpointing=False):
         if gradient_checkpointing and torch.is_grad_enabled():

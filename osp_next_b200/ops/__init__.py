@@ -62,10 +62,34 @@ def rms_norm(x, weight, eps: float = 1e-6):
 
 # ----------------------------------------------------------------------------- GEMMs
 
-def linear(x, weight, bias=None, act: Optional[str] = None, out_dtype=_BF16):
-    """``act(x·Wᵀ+b)`` on the tcgen05 GEMM (bf16 in, fp32 accumulate in TMEM)."""
+def _extra_pair(extra, M: int, N: int):
+    """Second GEMM operand pair (a2 [M,K2], b2 [N,K2]) as contiguous bf16 with K2 padded to
+    a multiple of 8 (zero columns), or None."""
+    if extra is None:
+        return None
+    a2, b2 = extra
+    a2 = _c(a2.reshape(M, -1).to(_BF16))
+    b2 = _c(b2.to(_BF16))
+    if a2.shape[1] % 8:
+        pk = 8 - a2.shape[1] % 8
+        a2 = torch.nn.functional.pad(a2, (0, pk))
+        b2 = torch.nn.functional.pad(b2, (0, pk))
+    if b2.shape[0] != N:
+        raise ValueError(f"second operand pair: b2 has {b2.shape[0]} rows, the GEMM has N = {N}")
+    return a2, b2
+
+
+def linear(x, weight, bias=None, act: Optional[str] = None, out_dtype=_BF16, extra=None):
+    """``act(x·Wᵀ [+ a2·b2ᵀ] + b)`` on the tcgen05 GEMM (bf16 in, fp32 accumulate in TMEM).
+    ``extra = (a2, b2)`` adds a second operand pair into the same accumulator (a LoRA
+    branch: a2 = x·Aᵀ, b2 = scaling·B)."""
     if not _cuda(x):
-        return ref.linear(x, weight, bias, act, out_dtype)
+        y = ref.linear(x, weight, bias, None, torch.float32)
+        if extra is not None:
+            y = y + extra[0].reshape(y.shape[:-1] + (-1,)).float() @ extra[1].float().t()
+        if act == "gelu_tanh":
+            y = torch.nn.functional.gelu(y, approximate="tanh")
+        return y.to(out_dtype)
     shp = x.shape
     a = _c(x.reshape(-1, shp[-1]).to(_BF16))
     w = _c(weight.to(_BF16))
@@ -82,7 +106,14 @@ def linear(x, weight, bias=None, act: Optional[str] = None, out_dtype=_BF16):
         w = torch.nn.functional.pad(w, (0, 0, 0, pn))
         b = None if b is None else torch.nn.functional.pad(b, (0, pn))
     out = torch.empty(a.shape[0], w.shape[0], dtype=out_dtype, device=x.device)
-    ext().gemm(a, w, b, out, 1 if act == "gelu_tanh" else 0, None, None, None, 0, 0)
+    pair = _extra_pair(extra, a.shape[0], N)
+    if pair is None:
+        ext().gemm(a, w, b, out, 1 if act == "gelu_tanh" else 0, None, None, None, 0, 0)
+    else:
+        a2, b2 = pair
+        if w.shape[0] != N:
+            b2 = torch.nn.functional.pad(b2, (0, 0, 0, w.shape[0] - N))
+        ext().gemm_dual(a, w, a2, b2, b, out, 1 if act == "gelu_tanh" else 0, None, None, None, 0, 0)
     if out.shape[1] != N:
         out = out[:, :N].contiguous()
     return out.view(*shp[:-1], N)
@@ -103,7 +134,7 @@ def gemm_t(a, b, a_mn: bool, b_mn: bool, out_dtype=torch.float32):
     return out
 
 
-def linear_gated_residual(x, weight, bias, resid, gate=None, dest_row=None, n_out=None, out=None):
+def linear_gated_residual(x, weight, bias, resid, gate=None, dest_row=None, n_out=None, out=None, extra=None):
     """``resid + (x·Wᵀ+b)·gate`` with fp32 residual, optional row remap on store.
 
     x [B,n,K] bf16, resid [B,n,C] fp32 (may alias ``out`` when no remap),
@@ -111,6 +142,16 @@ def linear_gated_residual(x, weight, bias, resid, gate=None, dest_row=None, n_ou
     at ``dest_row[m]`` of the [B,n_out,C] output (layout change fused in the store).
     """
     if not _cuda(x):
+        if extra is not None:
+            y = ref.linear(x, weight, bias, None, torch.float32)
+            y = y + extra[0].reshape(y.shape[:-1] + (-1,)).float() @ extra[1].float().t()
+            y = y * gate[:, None, :] if gate is not None else y
+            o = resid.float() + y
+            if dest_row is None:
+                return o
+            res = torch.zeros(o.shape[0], n_out, o.shape[2], dtype=o.dtype)
+            res[:, dest_row.long()] = o
+            return res
         return ref.linear_gated_residual(x, weight, bias, resid, gate, dest_row, n_out)
     B, n, K = x.shape
     a = _c(x.reshape(B * n, K).to(_BF16))
@@ -126,8 +167,13 @@ def linear_gated_residual(x, weight, bias, resid, gate=None, dest_row=None, n_ou
         if out is None:
             out = torch.empty(B, n_out, C, dtype=torch.float32, device=x.device)
         dr = dest_row.to(device=x.device, dtype=torch.int32).contiguous()
-    ext().gemm(a, w, None if bias is None else bias.float().contiguous(), out.view(-1, C), 0,
-               resid.view(-1, C), None if gate is None else gate.float().contiguous(), dr, n, n_out)
+    pair = _extra_pair(extra, B * n, C)
+    bb = None if bias is None else bias.float().contiguous()
+    gg = None if gate is None else gate.float().contiguous()
+    if pair is None:
+        ext().gemm(a, w, bb, out.view(-1, C), 0, resid.view(-1, C), gg, dr, n, n_out)
+    else:
+        ext().gemm_dual(a, w, pair[0], pair[1], bb, out.view(-1, C), 0, resid.view(-1, C), gg, dr, n, n_out)
     return out
 
 
@@ -155,12 +201,15 @@ def _chunks(n: int) -> int:
     return (n + _ROWS_PER_CTA - 1) // _ROWS_PER_CTA
 
 
-def linear_gelu_aux(x2, w, b):
-    """(gelu_tanh(x·Wᵀ+b), x·Wᵀ+b) both bf16, from one GEMM (FFN-up training forward)."""
+def linear_gelu_aux(x2, w, b, extra=None):
+    """(gelu_tanh(x·Wᵀ [+ a2·b2ᵀ] + b), the pre-activation) both bf16, from one GEMM (FFN-up
+    training forward; ``extra`` = a LoRA branch as a second operand pair)."""
     N = w.shape[0]
     out = torch.empty(x2.shape[0], N, dtype=_BF16, device=x2.device)
     aux = torch.empty_like(out)
-    ext().gemm_gelu_aux(_c(x2), _c(w.to(_BF16)), None if b is None else b.float().contiguous(), out, aux)
+    pair = _extra_pair(extra, x2.shape[0], N)
+    ext().gemm_gelu_aux(_c(x2), _c(w.to(_BF16)), None if b is None else b.float().contiguous(), out, aux,
+                        None if pair is None else pair[0], None if pair is None else pair[1])
     return out, aux
 
 

@@ -292,14 +292,17 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
           umma_bf16_ts(d, pa + 8u * k, sdesc_sw128(va + k * 2048, L::BOX, 1024), ID_PV, (acc || k > 0) ? 1u : 0u);
       };
       // wait for P_t(j) (in halves with kSplitP) and issue the PV MMAs
+      auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+        return mbar_wait(bar, parity, args.err, kErrAttnMma);
+      };
       auto pv = [&](int t, int j, int sV) -> bool {
         if (kSplitP) {
-          if (!mbar_wait(&p_half[t], j & 1, args.err, kErrAttnMma)) return false;
+          if (!wait(&p_half[t], j & 1)) return false;
           tc_fence_after();
           issue_pv(t, sV, 0, kKT / 32, j > 0);
           ATTN_TR(0, j, 4 * t + 0);
         }
-        if (!mbar_wait(&p_full[t], j & 1, args.err, kErrAttnMma)) return false;
+        if (!wait(&p_full[t], j & 1)) return false;
         tc_fence_after();
         issue_pv(t, sV, kSplitP ? kKT / 32 : 0, kKT / 16, j > 0);
         ATTN_TR(0, j, 4 * t + 1);
@@ -318,11 +321,11 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
         const int uV = 2 * j + 1, uK = 2 * j + 2;
         const int sV = uV % kSlots, sK = uK % kSlots;
         const bool more = j + 1 < n_kv;
-        if (!(ok = mbar_wait(&kv_full[sV], (uV / kSlots) & 1, args.err, kErrAttnMma))) break;
+        if (!(ok = wait(&kv_full[sV], (uV / kSlots) & 1))) break;
         if (!(ok = pv(0, j, sV))) break;
         if (!more) umma_commit(&o_done[0]);
         if (more) {
-          if (!(ok = mbar_wait(&kv_full[sK], (uK / kSlots) & 1, args.err, kErrAttnMma))) break;
+          if (!(ok = wait(&kv_full[sK], (uK / kSlots) & 1))) break;
           tc_fence_after();
           issue_s(0, sK);
           umma_commit(&s_full[0]);
@@ -354,7 +357,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      if (!(ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, args.err, kErrAttnSoftmax)))) break;
+      const bool got = mbar_wait(&s_full[t], j & 1, args.err, kErrAttnSoftmax);
+      if (!(ok = __all_sync(0xffffffffu, got))) break;
       tc_fence_after();
       if (lane == 0 && quarter == 0) ATTN_TR(1 + t, j, 0);
       const int n_valid = min(kKT, n_keys - j * kKT);
@@ -365,6 +369,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__
       tmem_ld_wait();
       if (lane == 0 && quarter == 0) ATTN_TR(1 + t, j, 1);
       float mx = full_tile ? attn_row_max<kKT, true>(sr, n_valid) : attn_row_max<kKT, false>(sr, n_valid);
+      if (lane == 0 && quarter == 0) ATTN_TR(1 + t, j, 5);
       mx *= sl2;
       const bool need = mx > m_ref + 8.0f;
       const float m_new = need ? mx : m_ref;

@@ -12,9 +12,13 @@ namespace osp {
 void gemm(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& bias, at::Tensor& out,
           int64_t act, const c10::optional<at::Tensor>& resid, const c10::optional<at::Tensor>& gate,
           const c10::optional<at::Tensor>& dest_row, int64_t rows_per_batch, int64_t n_out);
+void gemm_dual(const at::Tensor& a, const at::Tensor& b, const at::Tensor& a2, const at::Tensor& b2,
+               const c10::optional<at::Tensor>& bias, at::Tensor& out, int64_t act,
+               const c10::optional<at::Tensor>& resid, const c10::optional<at::Tensor>& gate,
+               const c10::optional<at::Tensor>& dest_row, int64_t rows_per_batch, int64_t n_out);
 void gemm_t(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, bool b_mn);
 void gemm_gelu_aux(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& bias, at::Tensor& out,
-                   at::Tensor& aux);
+                   at::Tensor& aux, const c10::optional<at::Tensor>& a2, const c10::optional<at::Tensor>& b2);
 void ln_modulate_bwd(const at::Tensor& x, const at::Tensor& dy, const at::Tensor& scale, at::Tensor& dx,
                      at::Tensor& dscale_part, at::Tensor& dshift_part, double eps);
 void gated_add_fwd(const at::Tensor& resid, const at::Tensor& y, const c10::optional<at::Tensor>& gate,
@@ -119,11 +123,14 @@ int64_t get_error(int64_t device, bool clear) {
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "OSP-Next B200 kernels (sm_100a: tcgen05 GEMM + flash attention, fused elementwise)";
   m.def("gemm", &osp::gemm);
+  m.def("gemm_dual", &osp::gemm_dual);
   m.def("ln_modulate", &osp::ln_modulate);
   m.def("rms_norm", &osp::rms_norm);
   m.def("qk_norm_rope", &osp::qk_norm_rope);
   m.def("gemm_t", &osp::gemm_t);
-  m.def("gemm_gelu_aux", &osp::gemm_gelu_aux);
+  m.def("gemm_gelu_aux", &osp::gemm_gelu_aux, pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("bias"),
+        pybind11::arg("out"), pybind11::arg("aux"), pybind11::arg("a2") = pybind11::none(),
+        pybind11::arg("b2") = pybind11::none());
   m.def("ln_modulate_bwd", &osp::ln_modulate_bwd);
   m.def("gated_add_fwd", &osp::gated_add_fwd);
   m.def("gated_add_bwd", &osp::gated_add_bwd);

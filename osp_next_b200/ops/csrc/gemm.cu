@@ -17,6 +17,10 @@
 //               store.  Two groups double the global loads in flight, which the residual
 //               epilogue (a streaming fp32 read-modify-write) needs to keep up with the MMAs.
 // Tiles are visited in M-groups of 16 so the weight stays L2-resident across a group.
+// Optionally a second operand pair (A2 [M,K2], B2 [N,K2]) is streamed after the first into
+// the same accumulator: D = A·Bᵀ + A2·B2ᵀ.  With A2 = x·Loraᵀ_A and B2 = s·Lora_B this is a
+// LoRA-adapted Linear in one GEMM, keeping every epilogue (bias, GELU, gated residual,
+// fused layout store) of the plain Linear.
 // Either operand may instead be MN-major (stored [K, M] / [K, N], MN contiguous): the
 // backward GEMMs dX = dY·W and dW = dYᵀ·X read dY, W and X in place, with no transposed
 // copies.  An MN-major tile is MN/64 TMA boxes of 64 K-rows × 64 elements (128B swizzle).
@@ -52,6 +56,7 @@ struct GemmArgs {
   const int64_t* out_ptrs;  // [world] peer output buffers (fused SSP exchange) or null
   const int* dest_rank;     // [rows_per_batch] owner rank of each row in the next layout
   __nv_bfloat16* aux;       // [M, N] bf16 pre-activation (store mode with GELU, training) or null
+  int K2;                   // K of the second operand pair (0: none)
   int* err;
 };
 
@@ -73,7 +78,8 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
 
 template <int BN, int MODE, typename OutT, bool A_MN = false, bool B_MN = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
+gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+            const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, GemmArgs args) {
   constexpr int STAGES = kSmemBudget / (kBM * kBK * 2 + BN * kBK * 2);
   constexpr uint32_t A_BYTES = kBM * kBK * 2;
   constexpr uint32_t B_BYTES = BN * kBK * 2;
@@ -101,7 +107,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   const int num_m = (args.M + kBM - 1) / kBM;
   const int num_n = (args.N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
-  const int num_kb = (args.K + kBK - 1) / kBK;
+  const int num_kb1 = (args.K + kBK - 1) / kBK;                 // k-blocks of the first pair
+  const int num_kb = num_kb1 + (args.K2 + kBK - 1) / kBK;       // ... and of both
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
@@ -111,6 +118,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if (args.K2 > 0) {
+      prefetch_tmap(&tmA2);
+      prefetch_tmap(&tmB2);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -132,19 +143,23 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, args.err, kErrGemmProducer)) { *abort_flag = 1; break; }
           mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
+          const bool second = kb >= num_kb1;
+          const CUtensorMap* ta = second ? &tmA2 : &tmA;
+          const CUtensorMap* tb = second ? &tmB2 : &tmB;
+          const int kc = (second ? kb - num_kb1 : kb) * kBK;   // K coordinate within the pair
           if constexpr (A_MN) {
 #pragma unroll
             for (int c = 0; c < kBM / 64; ++c)
-              tma_load_2d(&tmA, &full[stage], sA + stage * A_BYTES + c * MN_BOX, mb * kBM + 64 * c, kb * kBK);
+              tma_load_2d(ta, &full[stage], sA + stage * A_BYTES + c * MN_BOX, mb * kBM + 64 * c, kc);
           } else {
-            tma_load_2d(&tmA, &full[stage], sA + stage * A_BYTES, kb * kBK, mb * kBM);
+            tma_load_2d(ta, &full[stage], sA + stage * A_BYTES, kc, mb * kBM);
           }
           if constexpr (B_MN) {
 #pragma unroll
             for (int c = 0; c < BN / 64; ++c)
-              tma_load_2d(&tmB, &full[stage], sB + stage * B_BYTES + c * MN_BOX, nb * BN + 64 * c, kb * kBK);
+              tma_load_2d(tb, &full[stage], sB + stage * B_BYTES + c * MN_BOX, nb * BN + 64 * c, kc);
           } else {
-            tma_load_2d(&tmB, &full[stage], sB + stage * B_BYTES, kb * kBK, nb * BN);
+            tma_load_2d(tb, &full[stage], sB + stage * B_BYTES, kc, nb * BN);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -359,26 +374,37 @@ constexpr int gemm_smem_bytes() {
 }
 
 template <int BN, int MODE, typename OutT, bool A_MN = false, bool B_MN = false>
-static void launch_gemm(const at::Tensor& a, const at::Tensor& b, GemmArgs& args, cudaStream_t stream) {
+static void launch_gemm(const at::Tensor& a, const at::Tensor& b, GemmArgs& args, cudaStream_t stream,
+                        const at::Tensor* a2 = nullptr, const at::Tensor* b2 = nullptr) {
   // K-major operand: rows of K elements (box 64 K × tile rows); MN-major: rows of M/N
   // elements, one row per K index (box 64 MN × 64 K)
-  CUtensorMap tmA = A_MN ? make_tmap_2d_bf16(a.data_ptr(), args.M, args.K, a.stride(0), 64, kBK)
-                         : make_tmap_2d_bf16(a.data_ptr(), args.K, args.M, a.stride(0), kBK, kBM);
-  CUtensorMap tmB = B_MN ? make_tmap_2d_bf16(b.data_ptr(), args.N, args.K, b.stride(0), 64, kBK)
-                         : make_tmap_2d_bf16(b.data_ptr(), args.K, args.N, b.stride(0), kBK, BN);
+  auto map_a = [&](const at::Tensor& t, int K) {
+    return A_MN ? make_tmap_2d_bf16(t.data_ptr(), args.M, K, t.stride(0), 64, kBK)
+                : make_tmap_2d_bf16(t.data_ptr(), K, args.M, t.stride(0), kBK, kBM);
+  };
+  auto map_b = [&](const at::Tensor& t, int K) {
+    return B_MN ? make_tmap_2d_bf16(t.data_ptr(), args.N, K, t.stride(0), 64, kBK)
+                : make_tmap_2d_bf16(t.data_ptr(), K, args.N, t.stride(0), kBK, BN);
+  };
+  CUtensorMap tmA = map_a(a, args.K), tmB = map_b(b, args.K);
+  const bool dual = a2 != nullptr && args.K2 > 0;
+  CUtensorMap tmA2 = dual ? map_a(*a2, args.K2) : tmA;
+  CUtensorMap tmB2 = dual ? map_b(*b2, args.K2) : tmB;
+  if (!dual) args.K2 = 0;
   auto kern = gemm_kernel<BN, MODE, OutT, A_MN, B_MN>;
   constexpr int smem = gemm_smem_bytes<BN>();
   smem_opt_in(reinterpret_cast<const void*>(kern), smem);
   const int tiles = ((args.M + kBM - 1) / kBM) * ((args.N + BN - 1) / BN);
   const int grid = std::max(1, std::min(tiles, num_sms(a.get_device())));
-  kern<<<grid, kGemmThreads, smem, stream>>>(tmA, tmB, args);
+  kern<<<grid, kGemmThreads, smem, stream>>>(tmA, tmB, tmA2, tmB2, args);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-// out = act(a·bᵀ + bias)  or  out[remap] = resid + (a·bᵀ + bias)·gate
-void gemm(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& bias, at::Tensor& out,
-          int64_t act, const c10::optional<at::Tensor>& resid, const c10::optional<at::Tensor>& gate,
-          const c10::optional<at::Tensor>& dest_row, int64_t rows_per_batch, int64_t n_out) {
+// out = act(a·bᵀ [+ a2·b2ᵀ] + bias)  or  out[remap] = resid + (a·bᵀ [+ a2·b2ᵀ] + bias)·gate
+static void gemm_impl(const at::Tensor& a, const at::Tensor& b, const at::Tensor* a2, const at::Tensor* b2,
+                      const c10::optional<at::Tensor>& bias, at::Tensor& out, int64_t act,
+                      const c10::optional<at::Tensor>& resid, const c10::optional<at::Tensor>& gate,
+                      const c10::optional<at::Tensor>& dest_row, int64_t rows_per_batch, int64_t n_out) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "gemm: CUDA tensors expected");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm: bf16 operands");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1), "gemm: a [M,K], b [N,K]");
@@ -389,11 +415,23 @@ void gemm(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tens
               reinterpret_cast<uintptr_t>(b.data_ptr()) % 16 == 0, "gemm: 16-byte aligned operands");
   TORCH_CHECK(b.size(0) % 32 == 0, "gemm: N must be a multiple of 32");
   TORCH_CHECK(out.is_contiguous(), "gemm: contiguous output");
+  if (a2 != nullptr) {
+    TORCH_CHECK(b2 != nullptr && a2->is_cuda() && b2->is_cuda() && a2->scalar_type() == at::kBFloat16 &&
+                b2->scalar_type() == at::kBFloat16 && a2->dim() == 2 && b2->dim() == 2 &&
+                a2->size(0) == a.size(0) && b2->size(0) == b.size(0) && a2->size(1) == b2->size(1),
+                "gemm_dual: a2 [M,K2], b2 [N,K2] bf16");
+    TORCH_CHECK(a2->stride(1) == 1 && b2->stride(1) == 1 && a2->size(1) % 8 == 0 &&
+                (a2->stride(0) * 2) % 16 == 0 && (b2->stride(0) * 2) % 16 == 0 &&
+                reinterpret_cast<uintptr_t>(a2->data_ptr()) % 16 == 0 &&
+                reinterpret_cast<uintptr_t>(b2->data_ptr()) % 16 == 0,
+                "gemm_dual: K2-contiguous, K2 % 8 == 0, 16-byte aligned rows");
+  }
   c10::cuda::CUDAGuard guard(a.device());
   GemmArgs args{};
   args.M = (int)a.size(0);
   args.N = (int)b.size(0);
   args.K = (int)a.size(1);
+  args.K2 = a2 != nullptr ? (int)a2->size(1) : 0;
   args.bias = nullptr;
   if (bias.has_value()) {
     TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->is_contiguous() && bias->numel() == args.N,
@@ -428,27 +466,42 @@ void gemm(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tens
     } else {
       TORCH_CHECK(out.numel() == (int64_t)args.M * args.N, "gemm: out [M,N]");
     }
-    if (args.N % 256 == 0) launch_gemm<256, kEpiResidual, float>(a, b, args, stream);
-    else if (args.N % 128 == 0) launch_gemm<128, kEpiResidual, float>(a, b, args, stream);
-    else launch_gemm<64, kEpiResidual, float>(a, b, args, stream);
+    if (args.N % 256 == 0) launch_gemm<256, kEpiResidual, float>(a, b, args, stream, a2, b2);
+    else if (args.N % 128 == 0) launch_gemm<128, kEpiResidual, float>(a, b, args, stream, a2, b2);
+    else launch_gemm<64, kEpiResidual, float>(a, b, args, stream, a2, b2);
     return;
   }
   TORCH_CHECK(out.numel() == (int64_t)args.M * args.N, "gemm: out [M,N]");
   if (out.scalar_type() == at::kBFloat16) {
-    if (args.N % 256 == 0) launch_gemm<256, kEpiStore, __nv_bfloat16>(a, b, args, stream);
-    else if (args.N % 128 == 0) launch_gemm<128, kEpiStore, __nv_bfloat16>(a, b, args, stream);
-    else launch_gemm<64, kEpiStore, __nv_bfloat16>(a, b, args, stream);
+    if (args.N % 256 == 0) launch_gemm<256, kEpiStore, __nv_bfloat16>(a, b, args, stream, a2, b2);
+    else if (args.N % 128 == 0) launch_gemm<128, kEpiStore, __nv_bfloat16>(a, b, args, stream, a2, b2);
+    else launch_gemm<64, kEpiStore, __nv_bfloat16>(a, b, args, stream, a2, b2);
   } else {
     TORCH_CHECK(out.scalar_type() == at::kFloat, "gemm: out bf16 or f32");
-    if (args.N % 256 == 0) launch_gemm<256, kEpiStore, float>(a, b, args, stream);
-    else if (args.N % 128 == 0) launch_gemm<128, kEpiStore, float>(a, b, args, stream);
-    else launch_gemm<64, kEpiStore, float>(a, b, args, stream);
+    if (args.N % 256 == 0) launch_gemm<256, kEpiStore, float>(a, b, args, stream, a2, b2);
+    else if (args.N % 128 == 0) launch_gemm<128, kEpiStore, float>(a, b, args, stream, a2, b2);
+    else launch_gemm<64, kEpiStore, float>(a, b, args, stream, a2, b2);
   }
 }
 
+void gemm(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& bias, at::Tensor& out,
+          int64_t act, const c10::optional<at::Tensor>& resid, const c10::optional<at::Tensor>& gate,
+          const c10::optional<at::Tensor>& dest_row, int64_t rows_per_batch, int64_t n_out) {
+  gemm_impl(a, b, nullptr, nullptr, bias, out, act, resid, gate, dest_row, rows_per_batch, n_out);
+}
+
+// D = a·bᵀ + a2·b2ᵀ with the epilogues of gemm() (LoRA folded into the base GEMM).
+void gemm_dual(const at::Tensor& a, const at::Tensor& b, const at::Tensor& a2, const at::Tensor& b2,
+               const c10::optional<at::Tensor>& bias, at::Tensor& out, int64_t act,
+               const c10::optional<at::Tensor>& resid, const c10::optional<at::Tensor>& gate,
+               const c10::optional<at::Tensor>& dest_row, int64_t rows_per_batch, int64_t n_out) {
+  gemm_impl(a, b, &a2, &b2, bias, out, act, resid, gate, dest_row, rows_per_batch, n_out);
+}
+
 // Training forward of FFN-up: out = gelu_tanh(a·bᵀ + bias) and aux = a·bᵀ + bias (both bf16).
+// Optional second operand pair (a2, b2) accumulated into the same GEMM (LoRA FFN-up).
 void gemm_gelu_aux(const at::Tensor& a, const at::Tensor& b, const c10::optional<at::Tensor>& bias, at::Tensor& out,
-                   at::Tensor& aux) {
+                   at::Tensor& aux, const c10::optional<at::Tensor>& a2, const c10::optional<at::Tensor>& b2) {
   TORCH_CHECK(aux.is_cuda() && aux.scalar_type() == at::kBFloat16 && aux.is_contiguous() &&
               out.scalar_type() == at::kBFloat16 && aux.sizes() == out.sizes(), "gemm_gelu_aux: bf16 out/aux");
   TORCH_CHECK(a.is_cuda() && a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 && a.dim() == 2 &&
@@ -467,11 +520,23 @@ void gemm_gelu_aux(const at::Tensor& a, const at::Tensor& b, const c10::optional
   args.out = out.data_ptr();
   args.aux = reinterpret_cast<__nv_bfloat16*>(aux.data_ptr());
   args.err = error_word(a.get_device());
+  const at::Tensor* pa2 = nullptr;
+  const at::Tensor* pb2 = nullptr;
+  if (a2.has_value()) {
+    TORCH_CHECK(b2.has_value() && a2->scalar_type() == at::kBFloat16 && b2->scalar_type() == at::kBFloat16 &&
+                a2->dim() == 2 && b2->dim() == 2 && a2->size(0) == a.size(0) && b2->size(0) == b.size(0) &&
+                a2->size(1) == b2->size(1) && a2->stride(1) == 1 && b2->stride(1) == 1 && a2->size(1) % 8 == 0 &&
+                (a2->stride(0) * 2) % 16 == 0 && (b2->stride(0) * 2) % 16 == 0,
+                "gemm_gelu_aux: second pair a2 [M,K2], b2 [N,K2] bf16, K2 % 8 == 0");
+    pa2 = &*a2;
+    pb2 = &*b2;
+    args.K2 = (int)a2->size(1);
+  }
   if (args.M == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
-  if (args.N % 256 == 0) launch_gemm<256, kEpiStore, __nv_bfloat16>(a, b, args, stream);
-  else if (args.N % 128 == 0) launch_gemm<128, kEpiStore, __nv_bfloat16>(a, b, args, stream);
-  else launch_gemm<64, kEpiStore, __nv_bfloat16>(a, b, args, stream);
+  if (args.N % 256 == 0) launch_gemm<256, kEpiStore, __nv_bfloat16>(a, b, args, stream, pa2, pb2);
+  else if (args.N % 128 == 0) launch_gemm<128, kEpiStore, __nv_bfloat16>(a, b, args, stream, pa2, pb2);
+  else launch_gemm<64, kEpiStore, __nv_bfloat16>(a, b, args, stream, pa2, pb2);
 }
 
 template <bool A_MN, bool B_MN, typename OutT>

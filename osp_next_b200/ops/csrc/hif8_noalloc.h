@@ -21,6 +21,10 @@
 //    the GPU — on different streams without ordering — race on it; issue them in
 //    order on one stream.
 //  * No cudaMalloc / cudaFree or allocating library routine is called.
+//  * The looked-up scratch address is kept for the life of the process, per device
+//    ordinal.  Do not use the entry point across a device reset (cudaDeviceReset, or
+//    destroying and re-creating the primary context): the cached address would no
+//    longer be valid there.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>

@@ -77,7 +77,8 @@ class _HIF8MultiLinearFn(torch.autograd.Function):
     def forward(ctx, x, smf, smb, act, n, *wb):
         ws, bs = wb[:n], wb[n:]
         x_q = quant(x.to(torch.bfloat16).contiguous(), smf)
-        w_q = torch.cat([quant(w.detach().to(torch.bfloat16).contiguous(), smf) for w in ws], 0)
+        # each weight quantised in its own dtype, as HIF8Linear does, then bf16 for the GEMM
+        w_q = torch.cat([quant(w.detach().contiguous(), smf).to(torch.bfloat16) for w in ws], 0)
         has_b = all(b is not None for b in bs)
         b = torch.cat([b_.float() for b_ in bs], 0) if has_b else None
         x2 = x_q.reshape(-1, x.shape[-1])

@@ -563,6 +563,99 @@ def test_hif8_multi_linear_matches_separate_modules():
     h2 = torch.nn.functional.gelu(f(x).float(), approximate="tanh")
     (h2 * gh).sum().backward()
     assert _rel(h, h2) < 2e-2
-    for a, e in zip(got, (x.grad, f.weight.grad)):
+    mod = (x.grad.clone(), f.weight.grad.clone())
+    # Both paths quantise the GELU gradient to HiF8 but round it to bf16 at different
+    # points, which moves some elements across a quantisation step; so each is measured
+    # against the unquantised fp32 op and the fused path may not be clearly worse.
+    xf = x.detach().float().requires_grad_(True)
+    wf = f.weight.detach().float().requires_grad_(True)
+    h3 = torch.nn.functional.gelu(xf @ wf.t() + f.bias.detach().float(), approximate="tanh")
+    (h3 * gh).sum().backward()
+    for a, e, ref in zip(got, mod, (xf.grad, wf.grad)):
+        assert _rel(a, ref) <= 1.25 * _rel(e, ref) + 5e-3, (_rel(a, ref), _rel(e, ref))
+    _no_device_error()
+
+
+@pytest.mark.parametrize("K2", [32, 64, 192])
+def test_gemm_dual_operand_pair(K2):
+    """D = a·bᵀ + a2·b2ᵀ (a LoRA branch in the base GEMM's accumulator) with the store,
+    GELU and gated-residual (+ row remap) epilogues, against fp32."""
+    torch.manual_seed(27)
+    M, N, K = 700, 768, 512
+    x = torch.randn(M, K, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=DEV) / K ** 0.5).to(torch.bfloat16)
+    a2 = torch.randn(M, K2, device=DEV).to(torch.bfloat16)
+    b2 = (torch.randn(N, K2, device=DEV) / K2 ** 0.5).to(torch.bfloat16)
+    b = torch.randn(N, device=DEV)
+    exp = x.float() @ w.float().t() + a2.float() @ b2.float().t() + b
+    _close(ops.linear(x, w, b, None, out_dtype=torch.float32, extra=(a2, b2)), exp, 1e-4, 2e-3)
+    _close(ops.linear(x, w, b, "gelu_tanh", extra=(a2, b2)),
+           torch.nn.functional.gelu(exp, approximate="tanh"), 1e-2, 2e-2)
+    B, n = 2, M // 2
+    resid = torch.randn(B, n, N, device=DEV)
+    gate = torch.randn(B, N, device=DEV)
+    perm = torch.randperm(n, device=DEV)
+    y = ops.linear_gated_residual(x.view(B, n, K), w, b, resid.clone(), gate, dest_row=perm, n_out=n,
+                                  extra=(a2.view(B, n, K2), b2))
+    r = torch.empty_like(resid)
+    r[:, perm.long()] = resid + exp.view(B, n, N).to(torch.bfloat16).float() * gate[:, None]
+    _close(y, r, 1e-2, 6e-2)
+    _no_device_error()
+
+
+def test_lora_everywhere_fused_path_matches_autograd_path():
+    """LoRA on q/k/v/o (self and cross), FFN up/down: the no-grad path folds every branch into
+    the base GEMMs (dual operand pair, packed QKV, fused epilogues) and must agree with the
+    autograd path (separate LoRA GEMMs)."""
+    from osp_next_b200.models.lora import LoraModel
+    from osp_next_b200.models.osp_next import OSPNextModel
+    torch.manual_seed(0)
+    with torch.device(DEV):
+        m = OSPNextModel(dim=256, ffn_dim=512, num_heads=2, num_layers=4, text_len=16,
+                         skiparse_model_type="dual_end", sparse_ratio=2, num_full_blocks=0)
+    targets = ["self_attn.q", "self_attn.k", "self_attn.v", "self_attn.o", "cross_attn.q", "cross_attn.k",
+               "cross_attn.v", "cross_attn.o", "ffn.0", "ffn.2"]
+    net = LoraModel(m, r=16, lora_alpha=32, target_modules=targets)
+    for mod in net.lora_modules():
+        torch.nn.init.normal_(mod.lora_B["default"].weight, std=0.05)
+    x = torch.randn(1, 16, 3, 16, 16, device=DEV)
+    t = torch.tensor([400.0], device=DEV)
+    ctx = torch.randn(1, 16, 4096, device=DEV)
+    net.eval()
+    with torch.no_grad():
+        a = net(x, t, ctx)
+        with net.disable_adapter():
+            a0 = net(x, t, ctx)
+    net.train()
+    b = net(x, t, ctx).detach()
+    rel = (a - b).norm() / b.norm()
+    assert rel < 2e-2, rel
+    assert (a - a0).norm() / a0.norm() > 1e-3          # the adapters do change the output
+    _no_device_error()
+
+
+@pytest.mark.parametrize("act", [None, "gelu_tanh"])
+def test_lora_dual_gemm_autograd(act):
+    """LoRA on a frozen base through one dual GEMM (forward) and tcgen05 GEMMs (backward):
+    output and the gradients of A, B and x against fp32 autograd."""
+    from osp_next_b200.models.lora import LoraLinear
+    torch.manual_seed(28)
+    base = torch.nn.Linear(256, 512).to(DEV).requires_grad_(False)
+    m = LoraLinear(base, r=16, alpha=32).to(DEV)
+    with torch.no_grad():
+        m.lora_B["default"].weight.normal_(std=0.05)
+    x = torch.randn(3, 100, 256, device=DEV).to(torch.bfloat16).requires_grad_(True)
+    y = m(x, act=act)
+    g = torch.randn_like(y, dtype=torch.float32)
+    (y.float() * g).sum().backward()
+    A, Bm = m.lora_A["default"].weight, m.lora_B["default"].weight
+    got = (y.detach().float(), x.grad.clone(), A.grad.clone(), Bm.grad.clone())
+    x.grad = A.grad = Bm.grad = None
+    xf = x.float()
+    yr = xf @ base.weight.to(torch.bfloat16).float().t() + base.bias + m.scaling * (xf @ A.float().t()) @ Bm.float().t()
+    if act == "gelu_tanh":
+        yr = torch.nn.functional.gelu(yr, approximate="tanh")
+    (yr * g).sum().backward()
+    for a, e in zip(got, (yr.detach(), x.grad, A.grad, Bm.grad)):
         assert _rel(a, e) < 3e-2, _rel(a, e)
     _no_device_error()
