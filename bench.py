@@ -77,7 +77,7 @@ def parse():
     p.add_argument("--fsdp-comm", choices=["p2p", "nccl"], default="p2p",
                    help="train mode: FSDP block all-gather / reduce-scatter over NVLink peer memory or NCCL")
     p.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
-                   help="SSP layout exchange: fused GEMM-epilogue stores over NVLink, or NCCL all_to_all")
+                   help="SSP layout exchange and Ulysses all-to-all: NVLink peer memory (fused GEMM-epilogue stores at inference, staged pulls otherwise) or NCCL")
     return p.parse_args()
 
 
@@ -295,7 +295,8 @@ def train_config(args, world, out_dir):
                save_interval=10 ** 9, log_interval=1, fsdp_size=fsdp, skiparse_sp_size=ssp,
                use_skiparse_sequence_parallel=ssp > 1, sp_size=1, use_sequence_parallel=False,
                weight_dtype="bf16", gradient_checkpointing=True, seed=1024,
-               fsdp_p2p_collectives=getattr(args, "fsdp_comm", "p2p") == "p2p")
+               fsdp_p2p_collectives=getattr(args, "fsdp_comm", "p2p") == "p2p",
+               ssp_p2p_exchange=getattr(args, "exchange", "p2p") == "p2p")
     cfg["model_config"] = dict(cfg.get("model_config", {}), **{k: v for k, v in PRESETS[args.model].items()})
     cfg["model_config"].pop("pretrained_model_dir_or_checkpoint", None)
     if getattr(args, "quant", "none") == "hif8":

@@ -13,6 +13,16 @@ events after warm-up, max over ranks:
 
 Roofline of the fused path = max(GEMM FLOPs ÷ measured bf16 peak, bytes that leave the
 GPU ÷ 770 GB/s per direction); the line reports achieved = roofline ÷ p2p time.
+
+The exchange alone (the training path, where autograd keeps the result) is timed too:
+
+  staged       ``p2p_redistribute`` forward: stage the rows in peer memory, barrier, pull
+               this rank's next-layout rows into a fresh tensor
+  staged_bwd   its backward (gradient rows pulled back to their owners)
+  nccl_xchg    gather rows by destination, ``all_to_all_single``, scatter
+
+with roofline max(bytes that cross NVLink ÷ 770 GB/s, local HBM bytes ÷ measured copy
+bandwidth): HBM traffic is the stage copy (read + write) plus the pull's local writes.
 """
 from __future__ import annotations
 
@@ -37,6 +47,15 @@ def _peak_tflops() -> float:
         return float(d.get("bf16_tflops") or d.get("bf16_tflops_sustained"))
     except Exception:
         return 1400.0
+
+
+def _hbm_gbs() -> float:
+    p = os.path.join(os.path.dirname(__file__), "..", "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f).get("hbm_gbs"))
+    except Exception:
+        return 6650.0
 
 
 def main():
@@ -83,8 +102,31 @@ def main():
         dist.all_to_all_single(recv, send, rd.recv_counts, rd.send_counts)
         recv_buf[0].index_copy_(0, recv_rows, recv)
 
+    from osp_next_b200.parallel.p2p_collectives import p2p_redistribute
+    rt_x = torch.randn(1, n, C, device=dev, requires_grad=True)
+    g_out = torch.randn(1, lb.n_local, C, device=dev)
+    y_keep = [None]
+
+    def run_staged():
+        with torch.no_grad():
+            p2p_redistribute(rt_x, TOKEN, GROUP, grid, P, spec, ex)
+
+    def run_staged_fwd_for_bwd():
+        y_keep[0] = p2p_redistribute(rt_x, TOKEN, GROUP, grid, P, spec, ex)
+
+    def run_staged_bwd():
+        y_keep[0].backward(g_out, retain_graph=True)
+
+    def run_nccl_xchg():
+        send = out_local[0].index_select(0, send_rows)
+        recv = torch.empty(int(sum(rd.recv_counts)), C, device=dev)
+        dist.all_to_all_single(recv, send, rd.recv_counts, rd.send_counts)
+        recv_buf[0].index_copy_(0, recv_rows, recv)
+
     res = {}
-    for name, fn in (("local", run_local), ("p2p", run_p2p), ("nccl", run_nccl)):
+    run_staged_fwd_for_bwd()
+    for name, fn in (("local", run_local), ("p2p", run_p2p), ("nccl", run_nccl), ("staged", run_staged),
+                     ("staged_bwd", run_staged_bwd), ("nccl_xchg", run_nccl_xchg)):
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
@@ -107,7 +149,15 @@ def main():
     t_gemm = flops / (_peak_tflops() * 1e9)
     t_link = bytes_out / (NVLINK_GBS * 1e6)
     roof = max(t_gemm, t_link)
+    hbm = (2 * n + lb.n_local) * C * 4                   # stage read + write, pull writes
+    x_roof = max(t_link, hbm / (_hbm_gbs() * 1e6))
     if rank == 0:
+        print(json.dumps({"bench": "ssp_exchange_training", "world": world, "rows_per_rank": n,
+                          "ms_staged_fwd": round(res["staged"], 3), "ms_staged_bwd": round(res["staged_bwd"], 3),
+                          "ms_nccl_exchange": round(res["nccl_xchg"], 3), "roofline_ms": round(x_roof, 3),
+                          "frac_of_roofline_staged_fwd": round(x_roof / res["staged"], 3),
+                          "frac_of_roofline_staged_bwd": round(x_roof / res["staged_bwd"], 3),
+                          "frac_of_roofline_nccl": round(x_roof / res["nccl_xchg"], 3)}), flush=True)
         print(json.dumps({"bench": "ssp_exchange_ffn_down", "world": world, "rows_per_rank": n,
                           "remote_bytes_per_rank": bytes_out, "ms_local_gemm": round(res["local"], 3),
                           "ms_p2p_fused": round(res["p2p"], 3), "ms_nccl_path": round(res["nccl"], 3),

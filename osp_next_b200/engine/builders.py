@@ -58,6 +58,15 @@ def build_sp(config, num_heads: int) -> SPRuntime:
     return build_sp_groups(num_heads, skiparse_sp_size=ssp, sp_size=ul, cfg_size=cfg)
 
 
+def latent_grid(model, data_cfg, vae_stride=(4, 8, 8)):
+    """Patch grid (T, H, W) of the data config's samples: Wan VAE strides, then the
+    model's patch size."""
+    dc = data_cfg.get("dataset_config", {})
+    f, h, w = dc.get("sample_num_frames", 81), dc.get("sample_height", 480), dc.get("sample_width", 832)
+    pt, ph, pw = model.patch_size
+    return (((f - 1) // vae_stride[0] + 1) // pt, h // vae_stride[1] // ph, w // vae_stride[2] // pw)
+
+
 def build_model(config, dev=None, dtype=torch.float32):
     name = config.get("model_name", "osp_next")
     mcfg = dict(config.get("model_config", {}))

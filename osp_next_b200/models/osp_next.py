@@ -91,6 +91,8 @@ class BlockContext:
     next_n: int = 0
     relaid: bool = False              # set when the block stored its output in the next layout
     p2p: Optional[tuple] = None       # (peer pointer table, dest_rank, dest_row, n_stride): fused SSP exchange
+    exchange: object = None           # P2PExchange: Ulysses all-to-all over NVLink instead of NCCL
+    ulysses_grp: Optional[tuple] = None   # (size, my index, first rank, splits) of the Ulysses group
 
 
 class OSPNextSelfAttention(nn.Module):
@@ -170,7 +172,11 @@ class OSPNextSelfAttention(nn.Module):
     def forward(self, x, ctx: BlockContext):
         """x: modulated-normalised input [B, n_local, C] → attention output [B, n_local, C]."""
         q, k, v = self._qkv(x, ctx)
-        if ctx.ulysses_group is not None:
+        p2p_ul = ctx.ulysses_group is not None and ctx.exchange is not None and q.is_cuda
+        if p2p_ul:                    # one staged NVLink exchange for q, k and v
+            from ..parallel.p2p_collectives import p2p_ulysses_scatter
+            q, k, v = p2p_ulysses_scatter(ctx.exchange, ctx.ulysses_grp, q, k, v)
+        elif ctx.ulysses_group is not None:
             from ..parallel.comm import ulysses_all_to_all
             q = ulysses_all_to_all(q, ctx.ulysses_group, ctx.layout.a2a_splits, True)
             k = ulysses_all_to_all(k, ctx.ulysses_group, ctx.layout.a2a_splits, True)
@@ -180,7 +186,10 @@ class OSPNextSelfAttention(nn.Module):
             q, k, v = hif8_qkv(q, k, v, getattr(self, "scale_max_forward", 15.0),
                                getattr(self, "scale_max_backward", 224.0))
         o = Fn.attention(q, k, v, ctx.seg, ctx.seg)
-        if ctx.ulysses_group is not None:
+        if p2p_ul:
+            from ..parallel.p2p_collectives import p2p_ulysses_gather
+            (o,) = p2p_ulysses_gather(ctx.exchange, ctx.ulysses_grp, o)
+        elif ctx.ulysses_group is not None:
             from ..parallel.comm import ulysses_all_to_all
             o = ulysses_all_to_all(o, ctx.ulysses_group, ctx.layout.a2a_splits, False)
         return o.flatten(2)
@@ -563,15 +572,25 @@ class OSPNextModel(nn.Module):
         lay = make_layout(kind, grid, self.sparse_ratio, spec)
         pos = _dev(_layout_positions(kind, tuple(grid), self.sparse_ratio, spec), device, torch.int32)
         seg = lay.seg
-        ug = None
+        ug, ex, grp = None, None, None
         if lay.a2a_splits is not None and self.parallel is not None:
-            ug = self.parallel.full_group if kind == FULL or self.sparse_ratio == 1 else self.parallel.ulysses_group
-        return BlockContext(layout=lay, pos=pos, seg=seg, freqs=freqs, ulysses_group=ug)
+            dense = kind == FULL or self.sparse_ratio == 1
+            ug = self.parallel.full_group if dense else self.parallel.ulysses_group
+            ex = getattr(self.parallel, "p2p", None)
+            if ex is not None:
+                from ..parallel.p2p_collectives import ulysses_group_of
+                grp = ulysses_group_of(spec, dense) + (tuple(lay.a2a_splits),)
+        return BlockContext(layout=lay, pos=pos, seg=seg, freqs=freqs, ulysses_group=ug, exchange=ex,
+                            ulysses_grp=grp)
 
     def _redistribute(self, x, ka, kb, grid, spec):
         rd = make_redistribution(ka, kb, grid, self.sparse_ratio, spec)
         if spec.world == 1:
             return x if rd.identity else x[:, _dev(rd.gather, x.device, torch.long)]
+        ex = getattr(self.parallel, "p2p", None)
+        if ex is not None and x.is_cuda:
+            from ..parallel.p2p_collectives import p2p_redistribute
+            return p2p_redistribute(x, ka, kb, grid, self.sparse_ratio, spec, ex)
         from ..parallel.redistribute import redistribute
         return redistribute(x, rd, self.parallel.global_sp_group)
 

@@ -61,6 +61,8 @@ void p2p_close(int64_t ptr);
 void p2p_free(int64_t ptr);
 at::Tensor p2p_view(int64_t ptr, std::vector<int64_t> shape, at::ScalarType dtype, int64_t device);
 void p2p_barrier(const at::Tensor& flag_ptrs, int64_t rank, int64_t world, int64_t epoch, double limit_s);
+void p2p_pull(at::Tensor& out, const at::Tensor& ptrs, const at::Tensor& rank, const at::Tensor& off, int64_t R,
+              int64_t chunk_bytes, bool sum);
 void p2p_barrier_tagged(const at::Tensor& flag_ptrs, int64_t rank, int64_t world, int64_t epoch, int64_t tag,
                         double limit_s);
 void p2p_gather(const at::Tensor& bases, int64_t off, int64_t shard_bytes, int64_t rank, int64_t world,
@@ -155,6 +157,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_free", &osp::p2p_free);
   m.def("p2p_view", &osp::p2p_view);
   m.def("p2p_barrier", &osp::p2p_barrier);
+  m.def("p2p_pull", &osp::p2p_pull);
   m.def("p2p_barrier_tagged", &osp::p2p_barrier_tagged);
   m.def("p2p_gather", &osp::p2p_gather);
   m.def("p2p_reduce_scatter_f32", &osp::p2p_reduce_scatter_f32);

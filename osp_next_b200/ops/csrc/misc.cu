@@ -22,6 +22,15 @@ __device__ __forceinline__ void stf(T* p, long i, float v) { p[i] = static_cast<
 template <>
 __device__ __forceinline__ void stf<__nv_bfloat16>(__nv_bfloat16* p, long i, float v) { p[i] = __float2bfloat16(v); }
 
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16(v); }
+
 // x ← x + (u + g·(c − u))·dt   (fp32 math, stored in the latent dtype)
 template <typename TL, typename TP>
 __global__ void cfg_euler_kernel(const TL* __restrict__ lat, const TP* __restrict__ cond, const TP* __restrict__ unc,
@@ -70,10 +79,15 @@ __device__ __forceinline__ float hif8_round_dev(float v) {
   const int ae = abs(e);
   const int m = ae <= 3 ? 3 : (ae <= 7 ? 2 : (ae <= 15 ? 1 : 0));
   const int se = max(e, -22) - m;                          // step = 2^se
-  float q = floorf(ldexpf(a, -se) + 0.5f);
-  q = ldexpf(q, se);
+  // exact power-of-two scalings built from exponent bits: every finite |v| below the
+  // overflow threshold has se in [-25, 15], so 2^±se is a normal float (larger |v| and
+  // non-finite v are overwritten below)
+  const int sc = min(max(se, -100), 100);
+  float q = floorf(a * __int_as_float((127 - sc) << 23) + 0.5f);
+  q = q * __int_as_float((127 + sc) << 23);
   if (a < 1.1920928955078125e-07f) q = 0.f;                // 2^-23
   if (a >= 40960.f) q = __int_as_float(0x7f800000);
+  if (a != a) q = a;                                       // NaN stays NaN
   return copysignf(q, v);
 }
 
@@ -92,24 +106,54 @@ void hif8_round(const at::Tensor& x, at::Tensor& out, double s) {
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-// amax(|x|) as the bit pattern of a non-negative float (monotone as uint)
+// amax(|x|) as the bit pattern of a non-negative float (monotone as uint).  16-byte loads,
+// a block reduction, one atomic per block; the ragged tail (n mod 16/sizeof(T)) is
+// scalar.
 template <typename T>
-__global__ void absmax_kernel(const T* __restrict__ x, long n, unsigned* __restrict__ amax_bits) {
+__global__ void __launch_bounds__(256) absmax_kernel(const T* __restrict__ x, long n, unsigned* __restrict__ amax_bits) {
+  constexpr int V = 16 / sizeof(T);
+  const long nv = n / V;
+  const long tid = blockIdx.x * (long)blockDim.x + threadIdx.x, stride = (long)gridDim.x * blockDim.x;
   float m = 0.f;
-  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
-    m = fmaxf(m, fabsf(ldf(x, i)));
+  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  for (long i = tid; i < nv; i += stride) {
+    const uint4 r = __ldg(xv + i);
+    const T* e = reinterpret_cast<const T*>(&r);
+#pragma unroll
+    for (int k = 0; k < V; ++k) m = fmaxf(m, fabsf(to_f(e[k])));
+  }
+  for (long i = nv * V + tid; i < n; i += stride) m = fmaxf(m, fabsf(ldf(x, i)));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, __float_as_uint(m));
+  __shared__ float wm[8];
+  if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < (blockDim.x >> 5) ? wm[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (threadIdx.x == 0) atomicMax(amax_bits, __float_as_uint(m));
+  }
 }
 
 template <typename T>
-__global__ void hif8_qdq_kernel(const T* __restrict__ x, T* __restrict__ out, long n, const unsigned* amax_bits,
-                                float scale_max) {
+__global__ void __launch_bounds__(256) hif8_qdq_kernel(const T* __restrict__ x, T* __restrict__ out, long n,
+                                                       const unsigned* amax_bits, float scale_max) {
+  constexpr int V = 16 / sizeof(T);
   const float amax = fmaxf(__uint_as_float(*amax_bits), 1e-8f);    // x.abs().amax().clamp(min=1e-8)
   const float s = scale_max / amax;
-  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
-    stf(out, i, hif8_round_dev(ldf(x, i) * s) / s);
+  const long nv = n / V;
+  const long tid = blockIdx.x * (long)blockDim.x + threadIdx.x, stride = (long)gridDim.x * blockDim.x;
+  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  uint4* ov = reinterpret_cast<uint4*>(out);
+  for (long i = tid; i < nv; i += stride) {
+    uint4 r = __ldg(xv + i);
+    T* e = reinterpret_cast<T*>(&r);
+#pragma unroll
+    for (int k = 0; k < V; ++k) e[k] = from_f<T>(hif8_round_dev(to_f(e[k]) * s) / s);
+    ov[i] = r;
+  }
+  for (long i = nv * V + tid; i < n; i += stride) stf(out, i, hif8_round_dev(ldf(x, i) * s) / s);
 }
 
 // Per-tensor dynamic-scale HiF8 quantise→dequantise (hif8_linear.py:42-50 semantics).
@@ -121,6 +165,8 @@ void hif8_qdq(const at::Tensor& x, at::Tensor& out, double scale_max) {
   auto s = at::cuda::getCurrentCUDAStream();
   const long n = x.numel();
   if (!n) return;
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0 && (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0,
+              "hif8_qdq: 16-byte aligned tensors");
   auto amax = at::zeros({1}, x.options().dtype(at::kInt));
   unsigned* ab = reinterpret_cast<unsigned*>(amax.data_ptr<int>());
   if (x.scalar_type() == at::kBFloat16) {

@@ -20,6 +20,11 @@
 //    against every peer's) precedes a pull kernel: all-gather copies each peer's shard
 //    out of that peer's slot, reduce-scatter sums this rank's chunk of every peer's slot.
 //    A mismatched offset or a timeout sets an abort word that the pull kernel honours.
+//  * p2p_pull: the training SSP exchange and the Ulysses all-to-all.  Every rank stages its
+//    rows in a slot of peer memory, one p2p_barrier orders the stages, then every rank pulls
+//    exactly the chunks it owns from the ranks that hold them (a host-built table of
+//    (source rank, byte offset) per output chunk), summing several sources in fp32 where a
+//    row has replicas (the backward of a dense layout's replicated rows).
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -228,6 +233,68 @@ void p2p_reduce_scatter_f32(at::Tensor& out, const at::Tensor& bases, int64_t of
   p2p_reduce_scatter_f32_kernel<<<pull_grid(shard_elems / 4 + 1), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       out.data_ptr<float>(), bases.data_ptr<int64_t>(), off, shard_elems, (int)rank, (int)world, (float)scale,
       reinterpret_cast<const int*>(abort_ptr));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ---------------------------------------------------------------------------- table-driven pull
+// out chunk u (chunk_vecs 16-byte vectors, contiguous in `out`) = the chunk at
+// ptrs[rank[u·R + k]] + off[u·R + k]: copied (R == 1; rank < 0 → zeros) or the fp32 sum over
+// k (kSum; sources with rank < 0 are skipped, none → zeros).  One thread per 16-byte vector;
+// the chunk's table entries are warp-uniform whenever a chunk spans a warp.
+template <bool kSum>
+__global__ void __launch_bounds__(256) p2p_pull_kernel(int4* __restrict__ out, const int64_t* __restrict__ ptrs,
+                                                       const int* __restrict__ rank, const int64_t* __restrict__ off,
+                                                       int R, long n_chunks, int chunk_vecs) {
+  const long total = n_chunks * chunk_vecs;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long u = i / chunk_vecs;
+    const int v = (int)(i - u * chunk_vecs);
+    if (!kSum) {
+      const int r = __ldg(rank + u);
+      int4 val = make_int4(0, 0, 0, 0);
+      if (r >= 0) val = reinterpret_cast<const int4*>(reinterpret_cast<const char*>(ptrs[r]) + __ldg(off + u))[v];
+      out[i] = val;
+    } else {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k = 0; k < R; ++k) {
+        const int r = __ldg(rank + u * R + k);
+        if (r < 0) continue;
+        const int4 raw =
+            reinterpret_cast<const int4*>(reinterpret_cast<const char*>(ptrs[r]) + __ldg(off + u * R + k))[v];
+        acc.x += __int_as_float(raw.x); acc.y += __int_as_float(raw.y);
+        acc.z += __int_as_float(raw.z); acc.w += __int_as_float(raw.w);
+      }
+      out[i] = make_int4(__float_as_int(acc.x), __float_as_int(acc.y), __float_as_int(acc.z), __float_as_int(acc.w));
+    }
+  }
+}
+
+void p2p_pull(at::Tensor& out, const at::Tensor& ptrs, const at::Tensor& rank, const at::Tensor& off, int64_t R,
+              int64_t chunk_bytes, bool sum) {
+  TORCH_CHECK(out.is_cuda() && out.is_contiguous(), "p2p_pull: contiguous CUDA output");
+  TORCH_CHECK(chunk_bytes > 0 && chunk_bytes % 16 == 0, "p2p_pull: chunk size must be a multiple of 16 bytes");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0, "p2p_pull: output not 16-byte aligned");
+  const int64_t nbytes = out.numel() * out.element_size();
+  TORCH_CHECK(nbytes % chunk_bytes == 0, "p2p_pull: output is not a whole number of chunks");
+  const int64_t n_chunks = nbytes / chunk_bytes;
+  TORCH_CHECK(R >= 1 && rank.scalar_type() == at::kInt && off.scalar_type() == at::kLong &&
+              rank.numel() == n_chunks * R && off.numel() == n_chunks * R && rank.is_cuda() && off.is_cuda() &&
+              rank.is_contiguous() && off.is_contiguous(), "p2p_pull: int32 rank / int64 offset tables [chunks·R]");
+  TORCH_CHECK(ptrs.is_cuda() && ptrs.scalar_type() == at::kLong, "p2p_pull: int64 device table of slot pointers");
+  TORCH_CHECK(!sum || out.scalar_type() == at::kFloat, "p2p_pull: the summing pull is fp32");
+  TORCH_CHECK(sum || R == 1, "p2p_pull: a copying pull has one source per chunk");
+  c10::cuda::CUDAGuard guard(out.device());
+  if (n_chunks == 0) return;
+  const int vecs = (int)(chunk_bytes / 16);
+  const long work = n_chunks * vecs;
+  const int grid = (int)std::max<long>(1, std::min<long>((work + 255) / 256, 148L * 16));
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (sum)
+    p2p_pull_kernel<true><<<grid, 256, 0, st>>>(reinterpret_cast<int4*>(out.data_ptr()), ptrs.data_ptr<int64_t>(),
+                                                rank.data_ptr<int>(), off.data_ptr<int64_t>(), (int)R, n_chunks, vecs);
+  else
+    p2p_pull_kernel<false><<<grid, 256, 0, st>>>(reinterpret_cast<int4*>(out.data_ptr()), ptrs.data_ptr<int64_t>(),
+                                                 rank.data_ptr<int>(), off.data_ptr<int64_t>(), 1, n_chunks, vecs);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -80,16 +80,20 @@ def attach_sp(model, runtime: Optional[SPRuntime]):
     return model
 
 
-def enable_p2p_exchange(model, batch: int, grid, device):
-    """Turn on the fused NVLink SSP exchange for a model whose SP runtime is attached.
+def enable_p2p_exchange(model, batch: int, grid, device, limit_s: float = 2.0):
+    """Move the model's layout changes and Ulysses all-to-alls onto NVLink peer memory.
 
-    Buffers are sized for the largest per-rank row count over the model's layouts
-    (one common row stride), for ``batch`` samples of ``grid`` patches.
+    Inference stores FFN-down rows straight into the owners' residual slots when every
+    row has one owner (``full_sp == world``); every other exchange, and all of them under
+    autograd, is a staged pull.  Slots are sized for the largest per-rank row count over
+    the model's layouts, for ``batch`` samples of ``grid`` patches: fp32 residual rows,
+    and for staging bf16 q, k and v together (the largest staged exchange).  ``limit_s``
+    bounds each device barrier (a training step may wait on a slower rank for longer).
     """
     from ..models.layout import ParallelSpec, make_layout
     from .p2p import P2PExchange
     rt = getattr(model, "parallel", None)
-    if rt is None or rt.spec.world == 1 or rt.spec.full_sp != rt.spec.world:
+    if rt is None or rt.spec.world == 1:
         return None
     P = model.sparse_ratio
     n_stride = 0
@@ -97,5 +101,8 @@ def enable_p2p_exchange(model, batch: int, grid, device):
         for r in range(rt.spec.world):
             sp = ParallelSpec(rt.spec.ssp, rt.spec.ulysses, rt.spec.full_sp, r)
             n_stride = max(n_stride, make_layout(kind, tuple(grid), P, sp).n_local)
-    rt.p2p = P2PExchange(rt.global_sp_group, batch, n_stride, model.dim, device)
+    # q, k, v (or their gradients) in bf16: 3 × 2 bytes per element; a Ulysses member's
+    # share of the rows (Σ splits / size) never exceeds the largest n_local
+    stage = 6 * batch * n_stride * model.dim + 64
+    rt.p2p = P2PExchange(rt.global_sp_group, batch, n_stride, model.dim, device, stage_bytes=stage, limit_s=limit_s)
     return rt.p2p

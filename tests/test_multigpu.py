@@ -89,6 +89,86 @@ def test_ssp_matches_single_gpu(ssp, exchange):
             assert rel < 2e-2, (r, rel)
 
 
+def _train_model(device, heads):
+    from osp_next_b200.models.osp_next import OSPNextModel
+    torch.manual_seed(0)
+    with torch.device(device):
+        m = OSPNextModel(**dict(CFG, num_heads=heads))
+        m.head.head.weight.data.normal_(std=0.02)
+    return m.train()
+
+
+def _train_inputs(device):
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(*SHAPE, generator=g).to(device)
+    ctx = torch.randn(1, CFG["text_len"], 4096, generator=g).to(device)
+    tgt = torch.randn(*SHAPE, generator=g).to(device)
+    return x, torch.tensor([400.0], device=device), ctx, tgt
+
+
+def _train_step(m, dev):
+    x, t, ctx, tgt = _train_inputs(dev)
+    loss = (m(x, t, ctx).float() - tgt).pow(2).mean()
+    loss.backward()
+    return loss.detach(), {n: p.grad.float().cpu() for n, p in m.named_parameters() if p.grad is not None}
+
+
+def _train_sp_worker(rank, world, port, ssp, ul, heads, exchange, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    from osp_next_b200 import ops
+    from osp_next_b200.parallel.sp import attach_sp, build_sp_groups, enable_p2p_exchange
+    m = _train_model(dev, heads)
+    attach_sp(m, build_sp_groups(heads, skiparse_sp_size=ssp, sp_size=ul))
+    if exchange == "p2p":
+        enable_p2p_exchange(m, SHAPE[0], (SHAPE[2], SHAPE[3] // 2, SHAPE[4] // 2), dev, limit_s=30.0)
+    loss, grads = _train_step(m, dev)
+    torch.save({"loss": loss.item(), "grads": grads, "err": ops.ext().get_error(rank, True)},
+               os.path.join(out_dir, f"t{rank}.pt"))
+    if m.parallel is not None and m.parallel.p2p is not None:
+        m.parallel.p2p.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("ssp,ul,heads", [(2, 1, 4), (2, 2, 4), (4, 1, 2)])
+def test_training_sp_exchange_matches_single_gpu(ssp, ul, heads):
+    """One training step (forward + backward) under SSP, Ulysses × SSP and SSP with
+    replicated dense rows (full_sp < world), with the layout changes and head all-to-alls
+    over NVLink peer memory and over NCCL: the loss matches one GPU and the ranks'
+    gradients sum to world × the one-GPU gradient (the all-gather's SUM backward); the
+    two transports agree with each other more tightly."""
+    world = ssp * ul
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    m = _train_model("cuda:0", heads)
+    loss1, g1 = _train_step(m, torch.device("cuda:0"))
+    del m
+    torch.cuda.empty_cache()
+    res = {}
+    for exchange in ("nccl", "p2p"):
+        with tempfile.TemporaryDirectory() as d:
+            mp.start_processes(_train_sp_worker, args=(world, _port(), ssp, ul, heads, exchange, d), nprocs=world,
+                               join=True, start_method="spawn")
+            res[exchange] = [torch.load(os.path.join(d, f"t{r}.pt")) for r in range(world)]
+    for exchange, outs in res.items():
+        for o in outs:
+            assert o["err"] == 0
+            assert abs(o["loss"] - loss1.item()) <= 1e-2 * abs(loss1.item()), (exchange, o["loss"], loss1.item())
+        for n, g in g1.items():
+            s = sum(o["grads"][n] for o in outs) / world
+            rel = ((s - g).norm() / g.norm().clamp_min(1e-12)).item()
+            assert rel < 5e-2, (exchange, n, rel)
+    for n in g1:
+        a = sum(o["grads"][n] for o in res["p2p"])
+        b = sum(o["grads"][n] for o in res["nccl"])
+        rel = ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
+        assert rel < 1e-2, (n, rel)
+
+
 def _fsdp_worker(rank, world, port, out_dir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -112,14 +192,17 @@ def _fsdp_worker(rank, world, port, out_dir):
         opt = torch.optim.AdamW(m.parameters(), lr=1e-3)
         g = torch.Generator().manual_seed(10 + rank)
         losses = []
-        for _ in range(3):
-            x = torch.randn(1, 16, 3, 16, 16, generator=g).to(dev)
-            ctx = torch.randn(1, 16, 4096, generator=g).to(dev)
+        # no host synchronisation between steps: slot reuse in the NVLink arenas is ordered
+        # on the GPU alone
+        for _ in range(8):
+            x = torch.randn(1, 16, 3, 16, 16, generator=g).to(dev, non_blocking=True)
+            ctx = torch.randn(1, 16, 4096, generator=g).to(dev, non_blocking=True)
             loss = m(x, torch.tensor([400.0], device=dev), ctx).float().pow(2).mean()
             loss.backward()
             opt.step()
             opt.zero_grad()
-            losses.append(loss.item())
+            losses.append(loss.detach())
+        losses = [v.item() for v in losses]
         if arenas is not None:
             check(arenas, rank)
             dist.barrier()

@@ -96,6 +96,12 @@ def main(config, on_step=None):
         fsdp_dim = mesh["fsdp"] if "ddp" in (mesh.mesh_dim_names or ()) else mesh
         p2p_arenas = enable_p2p_fsdp(list(model.blocks), fsdp_dim.get_group(), device=dev,
                                      barrier_limit_s=config.get("fsdp_p2p_timeout_s", 60.0))
+    sp_p2p = None
+    if gsp > 1 and dev.type == "cuda" and config.get("ssp_p2p_exchange", True):
+        # SSP layout changes and Ulysses all-to-alls (forward and backward) over NVLink
+        from osp_next_b200.parallel.sp import enable_p2p_exchange
+        sp_p2p = enable_p2p_exchange(model, data_cfg.get("batch_size", 1), B.latent_grid(model, data_cfg), dev,
+                                     limit_s=config.get("ssp_p2p_timeout_s", 60.0))
     ema = FSDPEMAModel(model, config.get("ema_decay", 0.9999), config.get("ema_update_interval", 1)) \
         if config.get("ema_decay", 0) else None
     opt = FusedAdamW([p for p in model.parameters() if p.requires_grad], lr=opt_cfg.get("lr", 1e-5),
@@ -224,6 +230,8 @@ def main(config, on_step=None):
         from osp_next_b200.parallel.fsdp_comm import close
         dist.barrier()
         close(p2p_arenas)
+    if sp_p2p is not None:
+        sp_p2p.close()
     metrics.close()
     return step_times
 
