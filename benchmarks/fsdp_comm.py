@@ -1,9 +1,12 @@
 """Bandwidth of the NVLink pull all-gather / reduce-scatter used for FSDP, against NCCL.
 
 ``torchrun --nproc-per-node N -m benchmarks.fsdp_comm``: one 14B block's
-worth of data (351 M parameters: 702 MB bf16 gathered, 1.40 GB fp32 reduce-scattered),
-CUDA events on every rank, min of 5 after warm-up, max over ranks.  Roofline = bytes each
-rank pulls over NVLink ((N−1)/N of the buffer) ÷ 770 GB/s per direction.
+worth of data (351 M parameters: 702 MB bf16 gathered, 1.40 GB fp32 reduce-scattered, and
+the bf16-gradient reduce-scatter with fp32 accumulation that the bf16 blocks use: 702 MB
+pulled, fp32 shard out), CUDA events on every rank, min of 5 after warm-up, max over ranks.
+Roofline = bytes each rank pulls over NVLink ((N−1)/N of the buffer) ÷ 770 GB/s per
+direction.  The NCCL column of the bf16 case is what FSDP does without the fused pull: cast
+the bf16 gradients into an fp32 buffer, then an fp32 reduce-scatter.
 """
 from __future__ import annotations
 
@@ -47,7 +50,8 @@ def main():
     shard = (BLOCK_PARAMS + world - 1) // world
     shard = (shard + 63) // 64 * 64
     res = {"bench": "fsdp_collectives", "world": world, "params": shard * world}
-    for name, dtype in (("all_gather", torch.bfloat16), ("reduce_scatter", torch.float32)):
+    for name, dtype in (("all_gather", torch.bfloat16), ("reduce_scatter", torch.float32),
+                        ("reduce_scatter_bf16", torch.bfloat16)):
         esz = torch.empty(0, dtype=dtype).element_size()
         arena = _Arena(dist.group.WORLD, shard * world * esz, 2, dev)
         buf = arena.slot(shard * world, dtype)
@@ -62,6 +66,19 @@ def main():
 
             def nccl():
                 dist.all_gather_into_tensor(out_nccl, ref_in[rank * shard:(rank + 1) * shard])
+        elif name == "reduce_scatter_bf16":
+            out = torch.empty(shard, dtype=torch.float32, device=dev)
+
+            def p2p():
+                arena.barrier(off)
+                ops.ext().p2p_reduce_scatter_bf16(out, arena.bases, off, shard, arena.rank, world, 1.0 / world,
+                                                  arena.abort_ptr)
+            out_nccl = torch.empty(shard, dtype=torch.float32, device=dev)
+            staged = torch.empty(shard * world, dtype=torch.float32, device=dev)
+
+            def nccl():
+                staged.copy_(ref_in)
+                dist.reduce_scatter_tensor(out_nccl, staged, op=dist.ReduceOp.AVG)
         else:
             out = torch.empty(shard, dtype=dtype, device=dev)
 

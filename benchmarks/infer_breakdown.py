@@ -73,11 +73,13 @@ def main():
     ev = captured["events"]
     per = {c: 0.0 for c, _ in CATS}
     per["other"] = 0.0
+    by_name = {}
     comm_iv, comp_iv = [], []
     for e in ev:
         c = category(e.name)
         d = (e.time_range.end - e.time_range.start)
         per[c] += d
+        by_name[e.name] = by_name.get(e.name, 0.0) + d
         (comm_iv if c in ("nccl", "p2p") else comp_iv).append((e.time_range.start, e.time_range.end))
     steps = max(1, args.steps)
     busy = _union(comm_iv + comp_iv)
@@ -93,6 +95,8 @@ def main():
                "ms_per_step_by_category": {n: round(t[i].item(), 2) for i, n in enumerate(names)},
                "ms_device_busy": round(t[len(names)].item(), 2),
                "ms_exposed_comm": round(t[len(names) + 1].item(), 2),
+               "top_kernels_ms_per_step_rank0": [[k[:120], round(v / 1000.0 / steps, 3)] for k, v in
+                                                 sorted(by_name.items(), key=lambda kv: -kv[1])[:25]],
                "note": "max over ranks; from a profiled run"}
         print(json.dumps(rec), flush=True)
     if dist.is_initialized():

@@ -17,7 +17,9 @@ import statistics
 
 import torch
 
-from osp_next_b200.ops import attention, attention_bwd, gemm_t, linear, linear_gated_residual, ln_modulate, qk_norm_rope
+from osp_next_b200.ops import (adamw_, attention, attention_bwd, bias_grad, cfg_euler_step, gemm_t,
+                               hif8_quant_dequant, linear, linear_gated_residual, ln_modulate, qk_norm_rope,
+                               sde_step)
 from osp_next_b200.ops.reference import rope_freqs
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -136,6 +138,31 @@ def cases(size: str):
         fr = rope_freqs(D).to(dev)
         return (lambda: qk_norm_rope(qkv, wq, wk, pos, fr, H)), 0.0, B * N * C * 2 * 4
 
+    def hif8():
+        # per-tensor HiF8 quant-dequant of an FFN-input activation: amax pass + rounding pass
+        x = torch.randn(B * N, C, device=dev, dtype=bf)
+        return (lambda: hif8_quant_dequant(x, 15.0)), 0.0, x.numel() * 2 * 3
+
+    def biasg():
+        g = torch.randn(B * N, F, device=dev, dtype=bf)
+        return (lambda: bias_grad(g)), 0.0, g.numel() * 2
+
+    def cfg():
+        shape = (1, 16, 21, 96, 160)
+        lat, c, u = (torch.randn(shape, device=dev) for _ in range(3))
+        return (lambda: cfg_euler_step(lat, c, u, 5.0, -0.02)), 0.0, lat.numel() * 4 * 4
+
+    def sde():
+        shape = (12, 16, 9, 60, 104)             # Mix-GRPO rollout batch at 33f 480×832
+        x, v, nz = (torch.randn(shape, device=dev) for _ in range(3))
+        return (lambda: sde_step(x, v, 0.5, -0.02, 0.0, 1.0, noise=nz)), 0.0, x.numel() * 4 * 5
+
+    def adamw():
+        n = 351_000_000 // 8                      # one 14B block's shard at FSDP-8
+        p_, g_, m_, v_ = (torch.randn(n, device=dev) for _ in range(4))
+        v_.abs_()
+        return (lambda: adamw_(p_, g_, m_, v_, 1e-5, 0.9, 0.999, 1e-8, 0.01, 3, 0.5)), 0.0, n * 4 * 7
+
     M = B * N
     G = N // 4
     return {
@@ -152,6 +179,11 @@ def cases(size: str):
         "attn_dense_bwd": attn_bwd([N]),
         "ln_modulate": lnmod,
         "qk_norm_rope": qkrope,
+        "hif8_qdq": hif8,
+        "bias_grad": biasg,
+        "cfg_euler": cfg,
+        "sde_step": sde,
+        "adamw": adamw,
     }
 
 

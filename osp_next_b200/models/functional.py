@@ -86,10 +86,13 @@ class _LinearFn(torch.autograd.Function):
         dx = ops.gemm_t(gb, wb, a_mn=False, b_mn=True, out_dtype=dx_dtype)
         if dx is None:
             dx = ops.linear(gb, wb.t().contiguous(), None, None, out_dtype=torch.float32)
-        dw = ops.gemm_t(gb, x2, a_mn=True, b_mn=True, out_dtype=torch.float32)
+        # a bf16 weight takes its gradient in bf16 straight from the GEMM epilogue (the same
+        # fp32 accumulation rounded once), skipping an fp32 write and a conversion pass
+        dw_dtype = _BF16 if ctx.w_dtype == _BF16 else torch.float32
+        dw = ops.gemm_t(gb, x2, a_mn=True, b_mn=True, out_dtype=dw_dtype)
         if dw is None:
             dw = ops.linear(gb.t().contiguous(), x2.t().contiguous(), None, None, out_dtype=torch.float32)
-        db = g.float().sum(0) if ctx.has_b else None
+        db = ops.bias_grad(g) if ctx.has_b else None
         return dx.view(ctx.in_shape).to(ctx.x_dtype), dw.to(ctx.w_dtype), db, None
 
 

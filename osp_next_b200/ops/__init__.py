@@ -213,6 +213,18 @@ def linear_gelu_aux(x2, w, b, extra=None):
     return out, aux
 
 
+def bias_grad(g):
+    """Σ over rows of g [M, N] (the bias gradient of a Linear) in fp32, read straight from
+    bf16: per-chunk column sums on the GPU, then a sum over the chunks (deterministic)."""
+    g2 = g.reshape(-1, g.shape[-1])
+    if not _cuda(g2) or g2.shape[-1] % 8:
+        return g2.float().sum(0)
+    g2 = _c(g2.to(_BF16))
+    part = torch.empty((g2.shape[0] + 255) // 256, g2.shape[1], dtype=torch.float32, device=g2.device)
+    ext().bias_grad(g2, part)
+    return part.sum(0)
+
+
 def gelu_tanh_bwd(dh, pre):
     dpre = torch.empty_like(pre)
     ext().gelu_tanh_bwd(_c(dh.to(_BF16)), _c(pre), dpre)

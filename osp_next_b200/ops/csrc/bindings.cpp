@@ -29,6 +29,7 @@ void qk_norm_rope_bwd(const at::Tensor& raw, const at::Tensor& g, const at::Tens
                       const at::Tensor& freqs, at::Tensor& dqkv, at::Tensor& dw_part, int64_t part, int64_t B,
                       int64_t n, int64_t C, int64_t D, double eps);
 void gelu_tanh_bwd(const at::Tensor& dh, const at::Tensor& pre, at::Tensor& dpre);
+void bias_grad(const at::Tensor& g, at::Tensor& part);
 void rms_norm_bwd(const at::Tensor& x, const at::Tensor& dy, const c10::optional<at::Tensor>& w, at::Tensor& dx,
                   at::Tensor& dw_part, double eps);
 void ln_modulate(const at::Tensor& x, const c10::optional<at::Tensor>& shift, const c10::optional<at::Tensor>& scale,
@@ -68,6 +69,8 @@ void p2p_barrier_tagged(const at::Tensor& flag_ptrs, int64_t rank, int64_t world
 void p2p_gather(const at::Tensor& bases, int64_t off, int64_t shard_bytes, int64_t rank, int64_t world,
                 int64_t abort_ptr);
 void p2p_reduce_scatter_f32(at::Tensor& out, const at::Tensor& bases, int64_t off, int64_t shard_elems, int64_t rank,
+                            int64_t world, double scale, int64_t abort_ptr);
+void p2p_reduce_scatter_bf16(at::Tensor& out, const at::Tensor& bases, int64_t off, int64_t shard_elems, int64_t rank,
                             int64_t world, double scale, int64_t abort_ptr);
 
 static int* g_err[kMaxDevices] = {nullptr};
@@ -138,6 +141,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gated_add_bwd", &osp::gated_add_bwd);
   m.def("qk_norm_rope_bwd", &osp::qk_norm_rope_bwd);
   m.def("gelu_tanh_bwd", &osp::gelu_tanh_bwd);
+  m.def("bias_grad", &osp::bias_grad);
   m.def("rms_norm_bwd", &osp::rms_norm_bwd);
   m.def("attention_fwd", &osp::attention_fwd);
   m.def("attention_bwd", &osp::attention_bwd);
@@ -161,5 +165,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_barrier_tagged", &osp::p2p_barrier_tagged);
   m.def("p2p_gather", &osp::p2p_gather);
   m.def("p2p_reduce_scatter_f32", &osp::p2p_reduce_scatter_f32);
+  m.def("p2p_reduce_scatter_bf16", &osp::p2p_reduce_scatter_bf16);
   m.def("get_error", &osp::get_error, pybind11::arg("device"), pybind11::arg("clear") = true);
 }

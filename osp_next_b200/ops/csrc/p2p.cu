@@ -202,6 +202,45 @@ __global__ void p2p_reduce_scatter_f32_kernel(float* __restrict__ out, const int
   }
 }
 
+// Reduce-scatter of bf16 gradients with fp32 accumulation: out[i] (fp32) = scale · Σ_p
+// float(peer p's bf16 slot at off)[rank·S + i].  Casting each bf16 value to fp32 is exact,
+// so this is the fp32 reduce-scatter of the bf16 gradients (FSDP's reduce_dtype = fp32) with
+// the cast fused into the pull and half the bytes on NVLink.
+__global__ void p2p_reduce_scatter_bf16_kernel(float* __restrict__ out, const int64_t* bases, long off, long S,
+                                               int rank, int world, float scale, const int* abort_word) {
+  if (*reinterpret_cast<const volatile int*>(abort_word)) return;
+  const bool vec = (S % 8) == 0 && (off % 16) == 0;
+  const long n = vec ? S / 8 : S;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    if (vec) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int k = 0; k < world; ++k) {
+        const int p = (rank + 1 + k) % world;        // start at a different peer on every rank
+        const uint4 v = reinterpret_cast<const uint4*>(
+            reinterpret_cast<const char*>(bases[p]) + off + (long)rank * S * 2)[i];
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          acc[2 * e] += f.x;
+          acc[2 * e + 1] += f.y;
+        }
+      }
+      float4* o = reinterpret_cast<float4*>(out) + 2 * i;
+      o[0] = make_float4(acc[0] * scale, acc[1] * scale, acc[2] * scale, acc[3] * scale);
+      o[1] = make_float4(acc[4] * scale, acc[5] * scale, acc[6] * scale, acc[7] * scale);
+    } else {
+      float acc = 0.f;
+      for (int k = 0; k < world; ++k) {
+        const int p = (rank + 1 + k) % world;
+        acc += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(
+            reinterpret_cast<const char*>(bases[p]) + off + (long)rank * S * 2)[i]);
+      }
+      out[i] = acc * scale;
+    }
+  }
+}
+
 static int pull_grid(long work) {
   return (int)std::max<long>(1, std::min<long>((work + 255) / 256, 148L * 8));
 }
@@ -231,6 +270,19 @@ void p2p_reduce_scatter_f32(at::Tensor& out, const at::Tensor& bases, int64_t of
   c10::cuda::CUDAGuard guard(out.device());
   if (shard_elems == 0) return;
   p2p_reduce_scatter_f32_kernel<<<pull_grid(shard_elems / 4 + 1), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      out.data_ptr<float>(), bases.data_ptr<int64_t>(), off, shard_elems, (int)rank, (int)world, (float)scale,
+      reinterpret_cast<const int*>(abort_ptr));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void p2p_reduce_scatter_bf16(at::Tensor& out, const at::Tensor& bases, int64_t off, int64_t shard_elems,
+                             int64_t rank, int64_t world, double scale, int64_t abort_ptr) {
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.is_contiguous() && out.numel() == shard_elems,
+              "p2p_reduce_scatter_bf16: fp32 contiguous out [S]");
+  TORCH_CHECK(bases.scalar_type() == at::kLong && bases.numel() == world, "p2p_reduce_scatter_bf16: bases");
+  c10::cuda::CUDAGuard guard(out.device());
+  if (shard_elems == 0) return;
+  p2p_reduce_scatter_bf16_kernel<<<pull_grid(shard_elems / 8 + 1), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       out.data_ptr<float>(), bases.data_ptr<int64_t>(), off, shard_elems, (int)rank, (int)world, (float)scale,
       reinterpret_cast<const int*>(abort_ptr));
   C10_CUDA_KERNEL_LAUNCH_CHECK();

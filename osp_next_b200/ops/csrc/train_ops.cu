@@ -308,6 +308,44 @@ __global__ void gelu_tanh_bwd_kernel(const __nv_bfloat16* __restrict__ dh, const
   }
 }
 
+// ---------------------------------------------------------------------------- bias gradient
+// db = Σ_rows g for g bf16 [M, N] (N % 8 == 0): CTA (column block of 256, row chunk of
+// kBiasRows) → part[chunk, cols] fp32.  Each thread owns 8 adjacent columns (16-byte loads);
+// the 8 warps take interleaved rows and are combined through shared memory.
+constexpr int kBiasRows = 256;
+__global__ void __launch_bounds__(256) bias_grad_kernel(const __nv_bfloat16* __restrict__ g, float* __restrict__ part,
+                                                        long M, int N) {
+  __shared__ float red[8][257];
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  const int c0 = blockIdx.x * 256 + l * 8;
+  const long r0 = (long)blockIdx.y * kBiasRows;
+  const long r1 = min(M, r0 + kBiasRows);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (c0 < N) {
+#pragma unroll 4
+    for (long r = r0 + w; r < r1; r += 8) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(g + r * N + c0));
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        acc[2 * i] += f.x;
+        acc[2 * i + 1] += f.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) red[w][l * 8 + i] = acc[i];
+  __syncthreads();
+  const int c = blockIdx.x * 256 + threadIdx.x;
+  if (c < N) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s += red[k][threadIdx.x];
+    part[(long)blockIdx.y * N + c] = s;
+  }
+}
+
 // ---------------------------------------------------------------------------- RMSNorm
 // y = x̂·w, x̂ = x·rstd, rstd = rsqrt(mean(x²) + eps) over rows of C.
 // dx = rstd·(g − x̂·mean(g·x̂)) with g = dy·w;  dw_part[chunk] = Σ_rows dy·x̂.
@@ -503,6 +541,23 @@ void gelu_tanh_bwd(const at::Tensor& dh, const at::Tensor& pre, at::Tensor& dpre
   trn::gelu_tanh_bwd_kernel<<<ew_blocks(total4), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(dh.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(pre.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(dpre.data_ptr()), total4);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// g bf16 [M, N] contiguous (N % 8 == 0) → part fp32 [ceil(M / 256), N] column sums per row chunk
+void bias_grad(const at::Tensor& g, at::Tensor& part) {
+  TORCH_CHECK(g.is_cuda() && g.scalar_type() == at::kBFloat16 && g.is_contiguous() && g.dim() == 2,
+              "bias_grad: contiguous bf16 [M, N]");
+  const long M = g.size(0);
+  const int N = (int)g.size(1);
+  const long nchunk = (M + trn::kBiasRows - 1) / trn::kBiasRows;
+  TORCH_CHECK(N % 8 == 0 && part.scalar_type() == at::kFloat && part.is_contiguous() && part.numel() == nchunk * N,
+              "bias_grad: N % 8 and part fp32 [ceil(M/256), N]");
+  c10::cuda::CUDAGuard guard(g.device());
+  if (M == 0 || N == 0) return;
+  dim3 grid((unsigned)((N + 255) / 256), (unsigned)nchunk);
+  trn::bias_grad_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), part.data_ptr<float>(), M, N);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

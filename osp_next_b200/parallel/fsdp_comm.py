@@ -9,7 +9,11 @@ every peer, and the collective is a tagged device barrier plus one pull kernel
 (``ops/csrc/p2p.cu``):
 
 * all-gather: each rank copies every peer's shard out of that peer's slot over NVLink;
-* reduce-scatter (fp32 SUM / AVG): each rank sums its chunk of every peer's slot.
+* reduce-scatter (fp32 SUM / AVG): each rank sums its chunk of every peer's slot.  For
+  modules whose FSDP ``param_dtype`` is bf16 (the transformer blocks) the slot holds the bf16
+  gradients as autograd produced them and the pull kernel accumulates them in fp32: the
+  bf16→fp32 cast that FSDP's copy-in would do is fused into the reduce-scatter (exact, since
+  every bf16 value is an fp32 value) and half the bytes cross NVLink.
 
 FSDP allocates these buffers in the same order on every rank, so the ring of slots
 gives a slot the same offset everywhere; the barrier checks that (it carries the
@@ -161,17 +165,23 @@ class P2PAllGather(AllGather):
 
 class P2PReduceScatter(ReduceScatter):
     """fp32 SUM / AVG; FSDP allocates the input (world × shard, in the arena) and then the
-    output (shard, ordinary memory), in that order."""
+    output (shard, ordinary memory), in that order.  With ``grad_dtype=torch.bfloat16`` (the
+    module's FSDP param_dtype, so its gradients arrive in bf16) the input slot is bf16: FSDP's
+    copy-in then only copies, and the pull kernel sums the bf16 chunks in fp32 into the fp32
+    output that FSDP asked for."""
 
-    def __init__(self, arena: _Arena):
+    def __init__(self, arena: _Arena, grad_dtype: torch.dtype = torch.float32):
         self.arena = arena
+        self.grad_dtype = grad_dtype
         self._want_input = True
 
     def allocate(self, size, *, dtype, device):
         numel = math.prod(int(s) for s in size)
         if self._want_input:
             self._want_input = False
-            t = self.arena.slot(numel, dtype) if dtype == torch.float32 else None
+            t = None
+            if dtype == torch.float32:
+                t = self.arena.slot(numel, torch.bfloat16 if self.grad_dtype == torch.bfloat16 else dtype)
             return t if t is not None else torch.empty(numel, dtype=dtype, device=device)
         self._want_input = True
         return torch.empty(numel, dtype=dtype, device=device)
@@ -179,12 +189,15 @@ class P2PReduceScatter(ReduceScatter):
     def __call__(self, output_tensor, input_tensor, group, op, async_op=False):
         off = self.arena.offset(input_tensor)
         scale = {dist.ReduceOp.SUM: 1.0, dist.ReduceOp.AVG: 1.0 / self.arena.world}.get(op)
-        if off is None or scale is None or input_tensor.dtype != torch.float32:
+        if off is None or scale is None or input_tensor.dtype not in (torch.float32, torch.bfloat16):
+            if input_tensor.dtype != output_tensor.dtype:
+                input_tensor = input_tensor.to(output_tensor.dtype)
             return dist.reduce_scatter_tensor(output_tensor, input_tensor, op=op, group=group, async_op=async_op)
         a = self.arena
         a.barrier(off)
-        ops.ext().p2p_reduce_scatter_f32(output_tensor, a.bases, off, output_tensor.numel(), a.rank, a.world,
-                                         scale, a.abort_ptr)
+        pull = (ops.ext().p2p_reduce_scatter_bf16 if input_tensor.dtype == torch.bfloat16
+                else ops.ext().p2p_reduce_scatter_f32)
+        pull(output_tensor, a.bases, off, output_tensor.numel(), a.rank, a.world, scale, a.abort_ptr)
         return None
 
 
@@ -194,10 +207,21 @@ def _group_shard_numel(module) -> int:
     return sum(fp.padded_sharded_param_size.numel() for fp in pg.fsdp_params) if pg is not None else 0
 
 
+def _param_dtype(module) -> torch.dtype:
+    """The FSDP2 mixed-precision param_dtype of a module (its gradients' dtype); fp32 when
+    the module has no policy or the state cannot be read."""
+    try:
+        pol = module._get_fsdp_state()._mp_policy
+        return pol.param_dtype or torch.float32
+    except Exception:
+        return torch.float32
+
+
 def enable_p2p_fsdp(modules, group=None, nslots: int = 4, device=None, barrier_limit_s: float = 60.0):
     """Route the parameter all-gather and gradient reduce-scatter of the given FSDP2
     modules (the transformer blocks) through the NVLink pull kernels.  All modules share
-    one all-gather arena and one reduce-scatter arena sized for the largest of them.
+    one all-gather arena and one reduce-scatter arena sized for the largest of them; modules
+    with bf16 parameters reduce-scatter their bf16 gradients with fp32 accumulation.
     ``barrier_limit_s`` bounds each device barrier (a peer slower than that, e.g. stalled in
     data loading, makes the collective give up and record an error that the trainer's
     per-step check raises).  Returns the two arenas (call :func:`close` on them at exit)."""
@@ -208,11 +232,14 @@ def enable_p2p_fsdp(modules, group=None, nslots: int = 4, device=None, barrier_l
         return None
     n = max(_group_shard_numel(m) for m in mods)
     dev = device or torch.device("cuda", torch.cuda.current_device())
-    ag = _Arena(group, n * world * 2, nslots, dev, barrier_limit_s)    # bf16 parameters
-    rs = _Arena(group, n * world * 4, nslots, dev, barrier_limit_s)    # fp32 gradients
-    for m in mods:
+    grad_dtypes = [torch.bfloat16 if _param_dtype(m) == torch.bfloat16 else torch.float32 for m in mods]
+    gbytes = 2 if all(d == torch.bfloat16 for d in grad_dtypes) else 4
+    ag = _Arena(group, n * world * 2, nslots, dev, barrier_limit_s)        # bf16 parameters
+    rs = _Arena(group, n * world * gbytes, nslots, dev, barrier_limit_s)   # bf16 or fp32 gradients
+    rs.grad_bytes = gbytes
+    for m, gd in zip(mods, grad_dtypes):
         m.set_custom_all_gather(P2PAllGather(ag))
-        m.set_custom_reduce_scatter(P2PReduceScatter(rs))
+        m.set_custom_reduce_scatter(P2PReduceScatter(rs, grad_dtype=gd))
     return ag, rs
 
 

@@ -23,6 +23,12 @@ from .. import ops
 from ..ops import reference as ref
 
 
+def _out_dtype(dt: torch.dtype) -> torch.dtype:
+    """GEMM output dtype for a gradient whose tensor has dtype ``dt``: bf16 stays bf16
+    (rounded once from the fp32 accumulator), anything else is produced in fp32."""
+    return torch.bfloat16 if dt == torch.bfloat16 else torch.float32
+
+
 def quant(x: torch.Tensor, scale_max: float) -> torch.Tensor:
     """Scaled HiF8 quantise→dequantise of a whole tensor (device amax, no host sync)."""
     if x.is_cuda:
@@ -53,16 +59,19 @@ class _HIF8LinearFunction(torch.autograd.Function):
             wb, xb = w_q.to(torch.bfloat16), x2.to(torch.bfloat16)
             # operands read MN-major in place; transposed copies only where the shapes miss
             # the kernel's alignment rules
-            dx = ops.gemm_t(gb, wb, a_mn=False, b_mn=True)
+            # bf16 inputs / weights take their gradients in bf16 straight from the GEMM
+            # epilogue (fp32 accumulation rounded once, as the conversion would)
+            dx = ops.gemm_t(gb, wb, a_mn=False, b_mn=True, out_dtype=_out_dtype(x_q.dtype))
             if dx is None:
                 dx = ops.linear(gb, wb.t().contiguous(), None, out_dtype=torch.float32)
-            dw = ops.gemm_t(gb, xb, a_mn=True, b_mn=True)
+            dw = ops.gemm_t(gb, xb, a_mn=True, b_mn=True, out_dtype=_out_dtype(w_q.dtype))
             if dw is None:
                 dw = ops.linear(gb.t().contiguous(), xb.t().contiguous(), None, out_dtype=torch.float32)
+            db = ops.bias_grad(gb) if ctx.has_bias else None
         else:
             dx = g2 @ w_q
             dw = g2.t() @ x2
-        db = g2.float().sum(0) if ctx.has_bias else None
+            db = g2.float().sum(0) if ctx.has_bias else None
         return dx.view(x_q.shape).to(x_q.dtype), dw.to(w_q.dtype), db, None, None
 
 
@@ -109,14 +118,15 @@ class _HIF8MultiLinearFn(torch.autograd.Function):
             o += n_out
         gq = torch.cat(parts, 1) if len(parts) > 1 else parts[0]
         x2 = x_q.reshape(-1, x_q.shape[-1])
-        dx = ops.gemm_t(gq, w_q, a_mn=False, b_mn=True)
+        dx = ops.gemm_t(gq, w_q, a_mn=False, b_mn=True, out_dtype=_out_dtype(xdt))
         if dx is None:
             dx = ops.linear(gq, w_q.t().contiguous(), None, out_dtype=torch.float32)
-        dw = ops.gemm_t(gq, x2, a_mn=True, b_mn=True)
+        w_out = torch.bfloat16 if all(t == torch.bfloat16 for t in wdts) else torch.float32
+        dw = ops.gemm_t(gq, x2, a_mn=True, b_mn=True, out_dtype=w_out)
         if dw is None:
             dw = ops.linear(gq.t().contiguous(), x2.t().contiguous(), None, out_dtype=torch.float32)
         dws = list(dw.split(outs, 0))
-        dbs = list(gq.float().sum(0).split(outs, 0)) if has_b else [None] * len(outs)
+        dbs = list(ops.bias_grad(gq).split(outs, 0)) if has_b else [None] * len(outs)
         grads = [dx.view(xshape).to(xdt), None, None, None, None]
         grads += [d.to(t) for d, t in zip(dws, wdts)] + dbs
         return tuple(grads)

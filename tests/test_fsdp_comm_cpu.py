@@ -48,6 +48,51 @@ def test_reduce_scatter_allocates_input_in_arena_then_output_outside():
     assert a.offset(x) is None
 
 
+def test_reduce_scatter_bf16_gradients_use_a_bf16_slot():
+    # FSDP asks for an fp32 input (reduce_dtype); with bf16 gradients the slot is bf16, so
+    # the copy-in only copies and the pull kernel does the fp32 accumulation
+    a = FakeArena()
+    rs = fsdp_comm.P2PReduceScatter(a, grad_dtype=torch.bfloat16)
+    inp = rs.allocate((64,), dtype=torch.float32, device="cpu")
+    out = rs.allocate((32,), dtype=torch.float32, device="cpu")
+    assert inp.dtype == torch.bfloat16 and a.offset(inp) == 0
+    assert out.dtype == torch.float32 and a.offset(out) is None
+    # a non-fp32 reduce dtype never goes to the arena
+    x = rs.allocate((64,), dtype=torch.bfloat16, device="cpu")
+    assert a.offset(x) is None
+
+
+def test_reduce_scatter_fallback_casts_bf16_input_for_nccl(monkeypatch):
+    a = FakeArena()
+    rs = fsdp_comm.P2PReduceScatter(a, grad_dtype=torch.bfloat16)
+    seen = {}
+
+    def fake_rs(out, inp, op=None, group=None, async_op=False):
+        seen["dtype"] = inp.dtype
+        out.copy_(inp[:out.numel()])
+
+    monkeypatch.setattr(fsdp_comm.dist, "reduce_scatter_tensor", fake_rs)
+    inp = torch.ones(64, dtype=torch.bfloat16)          # outside the arena → c10d path
+    out = torch.zeros(32, dtype=torch.float32)
+    rs(out, inp, group=None, op=fsdp_comm.dist.ReduceOp.SUM)
+    assert seen["dtype"] == torch.float32 and torch.all(out == 1)
+
+
+def test_param_dtype_reads_the_fsdp_policy():
+    class Pol:
+        param_dtype = torch.bfloat16
+
+    class State:
+        _mp_policy = Pol()
+
+    class M:
+        def _get_fsdp_state(self):
+            return State()
+
+    assert fsdp_comm._param_dtype(M()) == torch.bfloat16
+    assert fsdp_comm._param_dtype(object()) == torch.float32
+
+
 def test_all_gather_slot_ring_and_oversize_fallback():
     a = FakeArena(slot_bytes=256, nslots=2)
     ag = fsdp_comm.P2PAllGather(a)

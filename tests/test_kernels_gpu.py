@@ -659,3 +659,14 @@ def test_lora_dual_gemm_autograd(act):
     for a, e in zip(got, (yr.detach(), x.grad, A.grad, Bm.grad)):
         assert _rel(a, e) < 3e-2, _rel(a, e)
     _no_device_error()
+
+
+@pytest.mark.parametrize("M,N", [(1, 8), (300, 1536), (14040, 8960), (257, 264)])
+def test_bias_grad_matches_fp32_sum(M, N):
+    torch.manual_seed(0)
+    g = torch.randn(M, N, device=DEV).to(torch.bfloat16)
+    db = ops.bias_grad(g)
+    assert db.dtype == torch.float32 and db.shape == (N,)
+    _close(db, g.double().sum(0), rtol=1e-5, atol=1e-3)
+    assert torch.equal(db, ops.bias_grad(g))          # deterministic
+    _no_device_error()

@@ -208,6 +208,8 @@ def _fsdp_worker(rank, world, port, out_dir):
             dist.barrier()
             close(arenas)
         out[mode] = (losses, sum(p.to_local().float().sum().item() for p in m.parameters()))
+        if arenas is not None:
+            out["rs_grad_bytes"] = arenas[1].grad_bytes     # bf16 blocks: bf16 reduce-scatter input
     torch.save(out, os.path.join(out_dir, f"f{rank}.pt"))
     dist.barrier()
     dist.destroy_process_group()
@@ -222,6 +224,51 @@ def test_fsdp_p2p_collectives_match_nccl():
         for r in range(2):
             o = torch.load(os.path.join(d, f"f{r}.pt"))
             (ln, pn), (lp, pp) = o["nccl"], o["p2p"]
+            assert o["rs_grad_bytes"] == 2
             for a, b in zip(ln, lp):
                 assert abs(a - b) <= 1e-4 * max(1.0, abs(a)), (ln, lp)
             assert abs(pn - pp) <= 1e-3 * max(1.0, abs(pn)), (pn, pp)
+
+
+def _rs_bf16_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    from osp_next_b200 import ops
+    from osp_next_b200.parallel.fsdp_comm import _Arena
+    res = {}
+    for shard in (4096, 1000, 77):                 # vector path, scalar path (shard % 8 != 0)
+        arena = _Arena(dist.group.WORLD, shard * world * 2, 2, dev)
+        buf = arena.slot(shard * world, torch.bfloat16)
+        g = torch.Generator(device=dev).manual_seed(100 + rank)
+        buf.copy_(torch.randn(shard * world, device=dev, generator=g).to(torch.bfloat16))
+        ref_in = buf.float().clone()
+        out = torch.empty(shard, dtype=torch.float32, device=dev)
+        arena.barrier(arena.offset(buf))
+        ops.ext().p2p_reduce_scatter_bf16(out, arena.bases, arena.offset(buf), shard, rank, world, 1.0 / world,
+                                          arena.abort_ptr)
+        ref = torch.empty(shard, dtype=torch.float32, device=dev)
+        dist.reduce_scatter_tensor(ref, ref_in, op=dist.ReduceOp.AVG)
+        torch.cuda.synchronize()
+        res[shard] = (out - ref).abs().max().item()
+        del buf
+        dist.barrier()
+        arena.close()
+    res["err"] = ops.ext().get_error(rank, True)
+    torch.save(res, os.path.join(out_dir, f"rs{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_p2p_reduce_scatter_bf16_matches_nccl_fp32():
+    """The bf16-gradient pull reduce-scatter (fp32 accumulation) equals NCCL's fp32
+    reduce-scatter of the same values cast to fp32, up to summation order."""
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_rs_bf16_worker, args=(2, _port(), d), nprocs=2, join=True, start_method="spawn")
+        for r in range(2):
+            o = torch.load(os.path.join(d, f"rs{r}.pt"))
+            assert o["err"] == 0
+            for shard in (4096, 1000, 77):
+                assert o[shard] <= 1e-6, o
