@@ -136,12 +136,38 @@ __global__ void __launch_bounds__(256) absmax_kernel(const T* __restrict__ x, lo
   }
 }
 
+// hif8_round_dev(v·s) / s without a division per element.  The rounded magnitude is
+// N·2^se with an integer N in [0, 16], and N·2^se is exact, so the quotient equals
+// RN(N / s)·2^se whenever that product is a normal float (scaling by a power of two commutes
+// with rounding there): tbl[N] = N / s is divided once per block.  Results near the
+// subnormal or overflow range, and every non-finite case, take the division itself, so the
+// output is bit-identical to hif8_round_dev(v·s) / s.
+__device__ __forceinline__ float hif8_qdq_elem(float v, float s, const float* tbl) {
+  const float y = v * s;
+  const float a = fabsf(y);
+  if (!(a >= 1.1920928955078125e-07f)) return a != a ? y : copysignf(0.f, y);       // NaN; below 2^-23 → ±0
+  if (a >= 40960.f) return copysignf(__int_as_float(0x7f800000), y);               // ±inf / s
+  const int e = (int)(__float_as_uint(a) >> 23) - 127;
+  const int ae = abs(e);
+  const int m = ae <= 3 ? 3 : (ae <= 7 ? 2 : (ae <= 15 ? 1 : 0));
+  const int se = max(e, -22) - m;                                   // in [-25, 15] here
+  const float N = floorf(a * __int_as_float((127 - se) << 23) + 0.5f);
+  const float p2 = __int_as_float((127 + se) << 23);
+  float r = tbl[(int)N] * p2;
+  if (r < 2.3509887e-38f || r > 8.507059e37f) r = (N * p2) / s;     // 2^-125 / 2^126: use the division
+  return copysignf(r, y);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) hif8_qdq_kernel(const T* __restrict__ x, T* __restrict__ out, long n,
                                                        const unsigned* amax_bits, float scale_max) {
   constexpr int V = 16 / sizeof(T);
   const float amax = fmaxf(__uint_as_float(*amax_bits), 1e-8f);    // x.abs().amax().clamp(min=1e-8)
   const float s = scale_max / amax;
+  __shared__ float tbl[17];
+  if (threadIdx.x < 17) tbl[threadIdx.x] = (float)threadIdx.x / s;
+  __syncthreads();
+  const bool fast = s > 0.f && s < 3.0e38f;                        // else (amax = inf) the plain form
   const long nv = n / V;
   const long tid = blockIdx.x * (long)blockDim.x + threadIdx.x, stride = (long)gridDim.x * blockDim.x;
   const uint4* xv = reinterpret_cast<const uint4*>(x);
@@ -149,11 +175,17 @@ __global__ void __launch_bounds__(256) hif8_qdq_kernel(const T* __restrict__ x, 
   for (long i = tid; i < nv; i += stride) {
     uint4 r = __ldg(xv + i);
     T* e = reinterpret_cast<T*>(&r);
+    if (fast) {
 #pragma unroll
-    for (int k = 0; k < V; ++k) e[k] = from_f<T>(hif8_round_dev(to_f(e[k]) * s) / s);
+      for (int k = 0; k < V; ++k) e[k] = from_f<T>(hif8_qdq_elem(to_f(e[k]), s, tbl));
+    } else {
+#pragma unroll
+      for (int k = 0; k < V; ++k) e[k] = from_f<T>(hif8_round_dev(to_f(e[k]) * s) / s);
+    }
     ov[i] = r;
   }
-  for (long i = nv * V + tid; i < n; i += stride) stf(out, i, hif8_round_dev(ldf(x, i) * s) / s);
+  for (long i = nv * V + tid; i < n; i += stride)
+    stf(out, i, fast ? hif8_qdq_elem(ldf(x, i), s, tbl) : hif8_round_dev(ldf(x, i) * s) / s);
 }
 
 // Per-tensor dynamic-scale HiF8 quantise→dequantise (hif8_linear.py:42-50 semantics).

@@ -670,3 +670,25 @@ def test_bias_grad_matches_fp32_sum(M, N):
     _close(db, g.double().sum(0), rtol=1e-5, atol=1e-3)
     assert torch.equal(db, ops.bias_grad(g))          # deterministic
     _no_device_error()
+
+
+@pytest.mark.parametrize("kind", ["all_bf16", "normal", "tiny", "large", "f32_heavy"])
+def test_hif8_qdq_bit_exact_against_reference(kind):
+    """The division-free quant-dequant kernel (table of N / s) gives exactly the reference's
+    Q(x·s)/s, bf16 and fp32, including values far from the bulk of the tensor."""
+    g = torch.Generator().manual_seed(3)
+    if kind == "all_bf16":
+        x = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+        x = x[torch.isfinite(x.float())]
+    elif kind == "f32_heavy":
+        x = torch.randn(1 << 20, generator=g) * torch.exp(torch.randn(1 << 20, generator=g) * 4)
+    else:
+        sc = {"normal": 1.0, "tiny": 1e-6, "large": 1e4}[kind]
+        x = (torch.randn(1 << 20, generator=g) * sc).to(torch.bfloat16)
+    for smax in (15.0, 224.0):
+        got = ops.hif8_quant_dequant(x.to(DEV), smax).cpu()
+        exp = ref.hif8_quant_dequant(x, smax)
+        assert got.dtype == exp.dtype
+        same = (got == exp) | (torch.isnan(got.float()) & torch.isnan(exp.float()))
+        assert bool(same.all()), (x[~same][:8], got[~same][:8], exp[~same][:8])
+    _no_device_error()

@@ -90,7 +90,7 @@ def main(config, on_step=None):
     if mesh is not None:
         B.fsdp_wrap(model, config, mesh, weight_dtype)
     p2p_arenas = None
-    if mesh is not None and dev.type == "cuda" and config.get("fsdp_p2p_collectives", False):
+    if mesh is not None and dev.type == "cuda" and config.get("fsdp_p2p_collectives", True):
         # block parameter all-gather / gradient reduce-scatter over NVLink peer memory
         from osp_next_b200.parallel.fsdp_comm import enable_p2p_fsdp
         fsdp_dim = mesh["fsdp"] if "ddp" in (mesh.mesh_dim_names or ()) else mesh
