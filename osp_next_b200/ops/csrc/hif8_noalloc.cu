@@ -4,7 +4,7 @@
 // array instead of allocated scratch:
 //   1. per-block max(|x|) over 4096-element slices → scratch[block]
 //   2. one block reduces the partial maxima       → scratch[kMaxPartials]
-//   3. elementwise rounding with s = scale_max / max(amax, 1e-8)
+//   3. elementwise rounding with s = (1 / max(amax, 1e-8)) · scale_max
 // Every word that stage 2 and 3 read is written by the previous stage of the same
 // call, so nothing needs clearing between calls.
 #include <cuda_bf16.h>
@@ -74,7 +74,7 @@ __global__ void reduce_partials(int nblocks, float* scratch) {
 }
 
 __global__ void quantize(const void* x, void* out, int dtype, int64_t n, float scale_max, const float* scratch) {
-  const float s = scale_max / fmaxf(scratch[kPartials], 1e-8f);
+  const float s = (1.0f / fmaxf(scratch[kPartials], 1e-8f)) * scale_max;   // as hif8_qdq computes it
   for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += (int64_t)gridDim.x * kThreads) {
     const float y = hif8_round_na(load_elem(x, dtype, i) * s) / s;
     if (dtype == 0) static_cast<float*>(out)[i] = y;

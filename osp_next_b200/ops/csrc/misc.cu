@@ -136,26 +136,47 @@ __global__ void __launch_bounds__(256) absmax_kernel(const T* __restrict__ x, lo
   }
 }
 
-// hif8_round_dev(v·s) / s without a division per element.  The rounded magnitude is
-// N·2^se with an integer N in [0, 16], and N·2^se is exact, so the quotient equals
-// RN(N / s)·2^se whenever that product is a normal float (scaling by a power of two commutes
-// with rounding there): tbl[N] = N / s is divided once per block.  Results near the
-// subnormal or overflow range, and every non-finite case, take the division itself, so the
-// output is bit-identical to hif8_round_dev(v·s) / s.
-__device__ __forceinline__ float hif8_qdq_elem(float v, float s, const float* tbl) {
+// hif8_round_dev(v·s) / s from the fp32 bits, without floor, conversions or a division per
+// element.  For |v·s| = a with exponent byte b, the HiF8 grid step is 2^(max(e,−22) − m), so
+// rounding half away from zero is "add half a step to the bits, clear the bits below the
+// step" (a carry into the exponent field gives the next power of two, which is on the grid):
+//   q_bits = (a_bits + half[b]) & mask[b]
+// with half = mask = 0 below 2^-23 (q = 0), and at b = 104 (a in [2^-23, 2^-22)) the fixed
+// result 2^-22.  Every q has at most three mantissa bits, so its top 11 bits index a table
+// of RN(q / s), one true division per entry per block; |a| ≥ 40960 → ±inf by a compare, and
+// exponent byte 255 (NaN) indexes NaN entries.  Bit-identical to hif8_round_dev(v·s) / s
+// (tests/test_kernels_gpu.py::test_hif8_qdq_bit_exact_against_reference).
+struct Hif8Tables {
+  uint32_t half[256], mask[256];
+  float val[2048];
+};
+
+__device__ __forceinline__ void hif8_tables_init(Hif8Tables* t, float s) {
+  for (int b = threadIdx.x; b < 256; b += blockDim.x) {
+    uint32_t h = 0u, m = 0u;
+    if (b == 104) { h = 1u << 23; m = 0xFF800000u; }
+    else if (b == 255) { h = 0u; m = 0xFFFFFFFFu; }
+    else if (b > 104) {
+      const int ae = abs(b - 127);
+      const int mb = ae <= 3 ? 3 : (ae <= 7 ? 2 : (ae <= 15 ? 1 : 0));
+      h = 1u << (22 - mb);
+      m = ~((1u << (23 - mb)) - 1u);
+    }
+    t->half[b] = h;
+    t->mask[b] = m;
+  }
+  for (int i = threadIdx.x; i < 2048; i += blockDim.x)
+    t->val[i] = i >= 2040 ? __int_as_float(0x7fc00000) : __uint_as_float((uint32_t)i << 20) / s;
+}
+
+__device__ __forceinline__ float hif8_qdq_elem(float v, float s, const Hif8Tables* t) {
   const float y = v * s;
-  const float a = fabsf(y);
-  if (!(a >= 1.1920928955078125e-07f)) return a != a ? y : copysignf(0.f, y);       // NaN; below 2^-23 → ±0
-  if (a >= 40960.f) return copysignf(__int_as_float(0x7f800000), y);               // ±inf / s
-  const int e = (int)(__float_as_uint(a) >> 23) - 127;
-  const int ae = abs(e);
-  const int m = ae <= 3 ? 3 : (ae <= 7 ? 2 : (ae <= 15 ? 1 : 0));
-  const int se = max(e, -22) - m;                                   // in [-25, 15] here
-  const float N = floorf(a * __int_as_float((127 - se) << 23) + 0.5f);
-  const float p2 = __int_as_float((127 + se) << 23);
-  float r = tbl[(int)N] * p2;
-  if (r < 2.3509887e-38f || r > 8.507059e37f) r = (N * p2) / s;     // 2^-125 / 2^126: use the division
-  return copysignf(r, y);
+  const uint32_t ab = __float_as_uint(y) & 0x7fffffffu;
+  const uint32_t b = ab >> 23;
+  const uint32_t q = (ab + t->half[b]) & t->mask[b];
+  float r = t->val[q >> 20];
+  if (__uint_as_float(ab) >= 40960.f) r = __int_as_float(0x7f800000);
+  return __uint_as_float(__float_as_uint(r) | (__float_as_uint(y) & 0x80000000u));
 }
 
 template <typename T>
@@ -163,9 +184,11 @@ __global__ void __launch_bounds__(256) hif8_qdq_kernel(const T* __restrict__ x, 
                                                        const unsigned* amax_bits, float scale_max) {
   constexpr int V = 16 / sizeof(T);
   const float amax = fmaxf(__uint_as_float(*amax_bits), 1e-8f);    // x.abs().amax().clamp(min=1e-8)
-  const float s = scale_max / amax;
-  __shared__ float tbl[17];
-  if (threadIdx.x < 17) tbl[threadIdx.x] = (float)threadIdx.x / s;
+  // `scale_max / x_max` with a Python number over a tensor is reciprocal-then-multiply in
+  // torch (Tensor.__rtruediv__), two roundings; the same here, so ties round alike
+  const float s = (1.0f / amax) * scale_max;
+  __shared__ Hif8Tables tb;
+  hif8_tables_init(&tb, s);
   __syncthreads();
   const bool fast = s > 0.f && s < 3.0e38f;                        // else (amax = inf) the plain form
   const long nv = n / V;
@@ -177,7 +200,7 @@ __global__ void __launch_bounds__(256) hif8_qdq_kernel(const T* __restrict__ x, 
     T* e = reinterpret_cast<T*>(&r);
     if (fast) {
 #pragma unroll
-      for (int k = 0; k < V; ++k) e[k] = from_f<T>(hif8_qdq_elem(to_f(e[k]), s, tbl));
+      for (int k = 0; k < V; ++k) e[k] = from_f<T>(hif8_qdq_elem(to_f(e[k]), s, &tb));
     } else {
 #pragma unroll
       for (int k = 0; k < V; ++k) e[k] = from_f<T>(hif8_round_dev(to_f(e[k]) * s) / s);
@@ -185,8 +208,11 @@ __global__ void __launch_bounds__(256) hif8_qdq_kernel(const T* __restrict__ x, 
     ov[i] = r;
   }
   for (long i = nv * V + tid; i < n; i += stride)
-    stf(out, i, fast ? hif8_qdq_elem(ldf(x, i), s, tbl) : hif8_round_dev(ldf(x, i) * s) / s);
+    stf(out, i, fast ? hif8_qdq_elem(ldf(x, i), s, &tb) : hif8_round_dev(ldf(x, i) * s) / s);
 }
+
+// every block builds the 10 KB rounding tables, so the grid stays at a few blocks per SM
+static int qdq_grid(long n) { return (int)std::min<long>((n / 8 + 255) / 256 + 1, 148L * 6); }
 
 // Per-tensor dynamic-scale HiF8 quantise→dequantise (hif8_linear.py:42-50 semantics).
 // The amax is reduced into a 4-byte device scratch word from the torch allocator.
@@ -204,12 +230,12 @@ void hif8_qdq(const at::Tensor& x, at::Tensor& out, double scale_max) {
   if (x.scalar_type() == at::kBFloat16) {
     auto* xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
     absmax_kernel<<<grid_for(n), 256, 0, s>>>(xp, n, ab);
-    hif8_qdq_kernel<<<grid_for(n), 256, 0, s>>>(xp, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), n, ab,
+    hif8_qdq_kernel<<<qdq_grid(n), 256, 0, s>>>(xp, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), n, ab,
                                                 (float)scale_max);
   } else {
     TORCH_CHECK(x.scalar_type() == at::kFloat, "hif8_qdq: f32/bf16");
     absmax_kernel<<<grid_for(n), 256, 0, s>>>(x.data_ptr<float>(), n, ab);
-    hif8_qdq_kernel<<<grid_for(n), 256, 0, s>>>(x.data_ptr<float>(), out.data_ptr<float>(), n, ab, (float)scale_max);
+    hif8_qdq_kernel<<<qdq_grid(n), 256, 0, s>>>(x.data_ptr<float>(), out.data_ptr<float>(), n, ab, (float)scale_max);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

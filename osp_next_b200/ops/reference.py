@@ -187,14 +187,15 @@ def cfg_euler_step(latents, cond, uncond, guidance: float, dt: float):
 def hif8_quant_dequant(x: torch.Tensor, scale_max: float = 15.0) -> torch.Tensor:
     """Per-tensor dynamic-scale HiF8 fake quantization (kernel semantics).
 
-    ``s = scale_max / amax(|x|)``; y = Q(x·s)/s where Q rounds to the HiF8 grid as
+    ``s = scale_max / amax(|x|)`` (as torch evaluates it: 1/amax, then times scale_max);
+    y = Q(x·s)/s where Q rounds to the HiF8 grid as
     the Ascend kernel does (quant_cy_npu/base/cusrc/hif8_quant_op.h:88-151):
     exponent e from the fp32 bits; mantissa bits 3/2/1/0 for |e| ≤ 3/7/15/else;
     step ``2^(max(e,−22) − m)``; round half away from zero; |v| < 2⁻²³ → 0;
     |v| ≥ 40960 → ±inf.  See :func:`hif8_round` for the grid alone.
     """
     amax = x.detach().abs().max().float().clamp(min=1e-8)
-    s = scale_max / amax
+    s = amax.reciprocal() * scale_max      # what torch makes of `scale_max / amax` (hif8_linear.py:46)
     y = hif8_round(x.float() * s) / s
     return y.to(x.dtype)
 

@@ -692,3 +692,39 @@ def test_hif8_qdq_bit_exact_against_reference(kind):
         same = (got == exp) | (torch.isnan(got.float()) & torch.isnan(exp.float()))
         assert bool(same.all()), (x[~same][:8], got[~same][:8], exp[~same][:8])
     _no_device_error()
+
+
+@pytest.mark.parametrize("B,n,C,K,R", [(2, 300, 512, 256, 3), (1, 1000, 5120, 640, 4), (2, 77, 1536, 512, 2)])
+def test_gemm_p2p_row_table_matches_local_store(B, n, C, K, R):
+    """The fused-exchange GEMM epilogue with a multi-destination (rank, row) table: R local
+    buffers stand in for the ranks' peer buffers, so the row-remap and pointer-table logic
+    is checked against the plain residual GEMM followed by an explicit scatter."""
+    torch.manual_seed(5)
+    x = torch.randn(B, n, K, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(C, K, device=DEV) / math.sqrt(K)).to(torch.bfloat16)
+    b = torch.randn(C, device=DEV)
+    resid = torch.randn(B, n, C, device=DEV)
+    gate = torch.randn(B, C, device=DEV)
+    dest_rank = torch.randint(0, R, (n,), device=DEV, dtype=torch.int32)
+    dest_row = torch.empty(n, dtype=torch.int32, device=DEV)
+    counts = []
+    for r in range(R):                                  # rows of rank r, in a shuffled order
+        idx = (dest_rank == r).nonzero().flatten()
+        dest_row[idx] = torch.randperm(idx.numel(), device=DEV).to(torch.int32)
+        counts.append(idx.numel())
+    n_stride = max(counts) + 3
+    bufs = [torch.full((B * n_stride, C), float("nan"), device=DEV) for _ in range(R)]
+    ptrs = torch.tensor([t.data_ptr() for t in bufs], dtype=torch.int64, device=DEV)
+    ops.linear_gated_residual_p2p(x, w, b, resid, gate, dest_rank, dest_row, ptrs, n_stride)
+    local = ops.linear_gated_residual(x, w, b, resid.clone(), gate)
+    torch.cuda.synchronize()
+    for r in range(R):
+        idx = (dest_rank == r).nonzero().flatten()
+        for bi in range(B):
+            got = bufs[r][bi * n_stride + dest_row[idx].long()]
+            assert torch.equal(got, local[bi, idx]), (r, bi)
+        untouched = torch.ones(B * n_stride, dtype=torch.bool, device=DEV)
+        for bi in range(B):
+            untouched[bi * n_stride + dest_row[idx].long()] = False
+        assert torch.isnan(bufs[r][untouched]).all()     # nothing written outside the table
+    _no_device_error()
