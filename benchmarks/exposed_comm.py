@@ -1,12 +1,14 @@
 """Exposed communication time of a training step (analysis tool, not a bench number).
 
 ``torchrun --nproc-per-node N -m benchmarks.exposed_comm [bench.py train flags]``
-runs the same trainer as ``bench.py --mode train`` and records, on every rank, the device
-kernels of the last two steps with the PyTorch profiler.  Per step:
+runs the same trainer as ``bench.py --mode train`` (``--impl reference``: the reference arm's
+training step, ``baseline/ref_train.py``) and records, on every rank, the device kernels of
+the timed steps with the PyTorch profiler.  Per step:
 
   busy     union of the intervals of all kernels
-  compute  union of the intervals of kernels that are not communication (NCCL kernels
-           and the NVLink barrier / pull kernels of the P2P collectives)
+  compute  union of the intervals of kernels that are not communication (NCCL kernels,
+           and the NVLink barrier / gather / reduce-scatter / pull kernels of the P2P
+           collectives and the SSP exchange)
   exposed  busy − compute: time in which only communication runs on the device
 
 The max over ranks is printed as one JSON line.  Timings come from a profiled run and are
@@ -23,7 +25,7 @@ import torch
 import torch.distributed as dist
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-COMM_MARKERS = ("nccl", "p2p_barrier", "p2p_gather", "p2p_reduce_scatter")
+COMM_MARKERS = ("nccl", "p2p_barrier", "p2p_gather", "p2p_reduce_scatter", "p2p_pull")
 
 
 def _union(iv):
@@ -54,7 +56,12 @@ def main():
                                   schedule=torch.profiler.schedule(wait=0, warmup=args.warmup - 1, active=args.steps,
                                                                    repeat=1))
     prof.start()
-    train_osp.main(cfg, on_step=lambda it, ms, tok: prof.step())
+    if args.impl == "reference":
+        sys.path.insert(0, os.path.join(ROOT, "baseline"))
+        import ref_train
+        ref_train.train(cfg, lambda it, ms, tok: prof.step())
+    else:
+        train_osp.main(cfg, on_step=lambda it, ms, tok: prof.step())
     prof.stop()
     kernels = [e for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
     comm = [(e.time_range.start, e.time_range.end) for e in kernels
@@ -67,8 +74,9 @@ def main():
                      dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     if rank == 0:
-        print(json.dumps({"bench": "exposed_comm_per_train_step", "model": args.model, "n_gpus": world,
-                          "fsdp_comm": args.fsdp_comm, "steps_profiled": args.steps,
+        print(json.dumps({"bench": "exposed_comm_per_train_step", "impl": args.impl, "model": args.model,
+                          "n_gpus": world, "fsdp_comm": args.fsdp_comm if args.impl == "ours" else "nccl",
+                          "steps_profiled": args.steps,
                           "ms_device_busy": round(t[0].item(), 2), "ms_compute": round(t[1].item(), 2),
                           "ms_exposed_comm": round(t[2].item(), 2), "ms_comm_kernels": round(t[3].item(), 2),
                           "note": "max over ranks; from a profiled run"}), flush=True)
